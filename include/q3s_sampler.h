@@ -1,0 +1,212 @@
+/*
+ * q3s_sampler.h — C ABI of the B200 token sampler for the Qwen3-TTS talker and
+ * code predictor (qwen3tts-rs 0.2.0, src/talker/sampling.rs).
+ *
+ * The reference sampler downloads every logit row to the host and samples it on
+ * one CPU thread.  This library samples rows where they already live (device
+ * memory) and returns only the token id and a status byte per row.  Every entry
+ * point below names the reference interface it replaces.
+ *
+ * Conventions
+ *   - Functions return Q3S_OK (0) or a negative Q3S_E_* code; the text of the
+ *     last failure on the calling thread is in q3s_last_error().
+ *   - Per-row sampling outcomes are Q3S_STATUS_* bytes (>= 0).  Their messages
+ *     (q3s_status_message) are the reference's error strings.
+ *   - "stream" is a cudaStream_t passed as void*; NULL is the legacy default
+ *     stream.  Batch calls are asynchronous on that stream.
+ *   - No torch types: plain pointers and sizes.
+ */
+#ifndef Q3S_SAMPLER_H
+#define Q3S_SAMPLER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Q3S_ABI_VERSION 1
+
+/* ---- return codes of API calls ------------------------------------------ */
+#define Q3S_OK 0
+#define Q3S_E_INVALID_ARGUMENT (-1)
+#define Q3S_E_CUDA (-2)
+#define Q3S_E_NO_DEVICE (-3)
+#define Q3S_E_OUT_OF_MEMORY (-4)
+#define Q3S_E_SAMPLING (-5) /* a single-row call whose row status is not OK */
+
+/* ---- per-row outcome (status byte) --------------------------------------
+ * Values and messages follow src/talker/sampling.rs:
+ *   INVALID_REPETITION_PENALTY  :281-285
+ *   INVALID_TEMPERATURE         :286-291
+ *   INVALID_TOP_P               :292-296
+ *   SUPPRESSION_NO_CANDIDATE    :642-647 (sampled) and :58-59 (greedy_select)
+ *   NO_CANDIDATE                :588-590 (greedy), :648-650, :705-708
+ *   INVALID_DENOMINATOR         :675-678, :715-718
+ * A row counts one Philox draw (its subsequence advances by one) exactly when
+ * do_sample is set and the status is OK (sampling.rs:298-305, 330-332).     */
+#define Q3S_STATUS_OK 0
+#define Q3S_STATUS_INVALID_REPETITION_PENALTY 1
+#define Q3S_STATUS_INVALID_TEMPERATURE 2
+#define Q3S_STATUS_INVALID_TOP_P 3
+#define Q3S_STATUS_SUPPRESSION_NO_CANDIDATE 4
+#define Q3S_STATUS_NO_CANDIDATE 5
+#define Q3S_STATUS_INVALID_DENOMINATOR 6
+#define Q3S_STATUS_UNSUPPORTED 7 /* vocabulary larger than Q3S_MAX_VOCAB */
+#define Q3S_STATUS_NOT_RUN 255   /* row was never reached (internal error) */
+
+/* Largest vocabulary one row may have (the codec vocabularies are 3072 and 2048). */
+#define Q3S_MAX_VOCAB 4096
+
+/* ---- element types of logits -------------------------------------------- */
+#define Q3S_DTYPE_F32 0
+#define Q3S_DTYPE_BF16 1 /* upcast exactly to f32 before any arithmetic */
+
+/* "None" for suppress_from / allow_suppressed_token. */
+#define Q3S_NONE (-1)
+
+/* Mirrors SamplingOptions (sampling.rs:19-25).  The f64 fields keep the
+ * reference's f64 validation and comparisons (rp != 1.0, top_p < 1.0); the
+ * kernel casts to f32 where the reference does (`as f32`). */
+typedef struct q3s_sampling_options {
+  double temperature;
+  uint64_t top_k; /* 0 = off */
+  double top_p;
+  double repetition_penalty;
+} q3s_sampling_options;
+
+/* Per-row parameters of a batched call (device memory, 48 bytes).
+ * suppress_from / allow_token: Q3S_NONE for None; values beyond the row's
+ * vocabulary are legal and behave as in the reference. */
+typedef struct q3s_row_params {
+  double temperature;
+  double top_p;
+  double repetition_penalty;
+  uint32_t top_k;        /* 0 = off; values >= vocabulary keep every candidate */
+  uint32_t do_sample;    /* 0 = greedy argmax over raw logits (sampling.rs:576-591) */
+  int32_t suppress_from; /* Q3S_NONE or index */
+  int32_t allow_token;   /* Q3S_NONE or index */
+  uint32_t ctr_lo;       /* Philox counter word 0; the reference's Sampler keeps it 0 */
+  uint32_t reserved;
+} q3s_row_params;
+
+/* One batched sampling launch.  All pointers are device pointers unless noted.
+ *
+ * Row r's logits start at element row_offsets[r] (or r*row_stride when
+ * row_offsets is NULL) and hold row_vocab[r] (or vocab) elements.  Its
+ * parameters are params[r*params_stride] (params_stride 0 broadcasts one
+ * struct).  Its history is history[history_offsets[r] .. history_offsets[r+1])
+ * (no history when history_offsets is NULL).  Its Philox key/counter are
+ * seeds[r] / subseqs[r]. */
+typedef struct q3s_batch {
+  const void* logits;
+  int32_t dtype;
+  int32_t vocab;
+  int64_t num_rows;
+  int64_t row_stride;
+  const int64_t* row_offsets;     /* [num_rows] or NULL */
+  const int32_t* row_vocab;       /* [num_rows] or NULL */
+  const q3s_row_params* params;   /* [num_rows] or [1] */
+  int64_t params_stride;          /* 0 or 1 */
+  const uint64_t* seeds;          /* [num_rows] */
+  const uint64_t* subseqs;        /* [num_rows] */
+  const uint16_t* history;        /* concatenated c0 history ids */
+  const int64_t* history_offsets; /* [num_rows + 1] or NULL */
+  uint32_t* tokens;               /* out [num_rows] */
+  uint8_t* status;                /* out [num_rows] */
+  /* Optional, for testing and debugging (NULL in production):            */
+  const float* uniform_override;  /* [num_rows]: use this draw instead of Philox */
+  float* probs;                   /* out [num_rows * probs_stride]: final softmax over survivors */
+  uint8_t* masks;                 /* out [num_rows * probs_stride]: bit0 candidate, bit1 top-k, bit2 top-p */
+  int64_t probs_stride;
+} q3s_batch;
+
+/* ---- library / context --------------------------------------------------- */
+typedef struct q3s_context q3s_context;
+
+int q3s_abi_version(void);
+const char* q3s_last_error(void);
+const char* q3s_status_message(int status);
+
+/* One context per (device, host thread).  Holds the launch configuration and
+ * small staging buffers for single-row calls. */
+int q3s_context_create(int device, q3s_context** out);
+void q3s_context_destroy(q3s_context* ctx);
+
+/* Batched sampling: the fused penalty / mask / temperature / top-k / top-p /
+ * Philox-draw kernel over many rows.  Replaces, per row, one call of
+ * Sampler::sample_with_mode_and_transfer_observer (sampling.rs:247-334) minus
+ * its host download (sampling.rs:273).  Does not advance any counter: the
+ * caller advances subseq for rows whose status is OK and do_sample is set. */
+int q3s_sample_batch(q3s_context* ctx, const q3s_batch* batch, void* stream);
+
+/* Greedy argmax with the talker reserved-token mask, many rows, on device.
+ * mode Q3S_GREEDY_SELECT follows greedy_select (sampling.rs:40-60): first
+ * index of the IEEE maximum over finite allowed entries; status
+ * SUPPRESSION_NO_CANDIDATE when none.  mode Q3S_GREEDY_ON_DEVICE follows
+ * greedy_select_on_device (sampling.rs:72-117): the token is vocab (the
+ * sentinel) when no finite candidate remains, status stays OK; ties resolve to
+ * the lowest index (the contract stated at sampling.rs:70-71). */
+#define Q3S_GREEDY_SELECT 0
+#define Q3S_GREEDY_ON_DEVICE 1
+int q3s_greedy_batch(q3s_context* ctx, const void* logits, int32_t dtype, int64_t num_rows,
+                     int64_t row_stride, int32_t vocab, int64_t suppress_from,
+                     int64_t allow_token, int32_t mode, uint32_t* tokens, uint8_t* status,
+                     void* stream);
+
+/* ---- stateful sampler: the drop-in for `Sampler` ------------------------ */
+/* Mirrors Sampler (sampling.rs:144-335): one Philox stream (seed, subsequence
+ * counter) shared by the talker and code-predictor calls of one request. */
+typedef struct q3s_sampler q3s_sampler;
+
+typedef struct q3s_sampler_diagnostics { /* SamplerDiagnostics, sampling.rs:27-37 */
+  uint32_t call_count;
+  uint32_t sampled_calls;
+  uint32_t greedy_calls;
+  uint32_t history_nonempty_calls;
+  uint8_t history_nonempty_sequence[64];
+  uint8_t sequence[64];
+  uint64_t sequence_len;
+} q3s_sampler_diagnostics;
+
+/* Transfer observer (TransferObserver, src/alignment_stage_dump.rs:40-51).
+ * The device sampler moves one token per call instead of the full logit
+ * vector; the event reports what crossed the device boundary. */
+#define Q3S_TRANSFER_SAMPLED_TOKEN 0 /* 1 element device->host per call */
+typedef void (*q3s_transfer_callback)(void* user_data, int32_t direction, int32_t event,
+                                      uint64_t elements);
+
+/* Sampler::new (sampling.rs:158-170). */
+int q3s_sampler_create(q3s_context* ctx, uint64_t seed, q3s_sampler** out);
+void q3s_sampler_destroy(q3s_sampler* s);
+/* Sampler::subsequence_counter (sampling.rs:174); the setter supports resume
+ * from a saved (seed, subsequence) pair. */
+uint64_t q3s_sampler_subsequence_counter(const q3s_sampler* s);
+void q3s_sampler_set_subsequence_counter(q3s_sampler* s, uint64_t subseq);
+/* Sampler::diagnostics (sampling.rs:179). */
+int q3s_sampler_diagnostics(const q3s_sampler* s, q3s_sampler_diagnostics* out);
+
+/* Sampler::sample_with_mode_and_transfer_observer (sampling.rs:247-334).
+ * logits: device pointer to n elements of dtype.  history: HOST pointer to
+ * hist_len u16 ids (the c0 history).  suppress_from / allow_token: Q3S_NONE
+ * for None.  Returns Q3S_OK with *token set, Q3S_E_SAMPLING with *row_status
+ * set to the reference error, or another negative code.  Synchronises the
+ * stream to read the token (4 bytes + 1 status byte). */
+int q3s_sampler_sample_with_mode(q3s_sampler* s, const void* logits, int32_t dtype, int64_t n,
+                                 const q3s_sampling_options* options, int32_t do_sample,
+                                 int64_t suppress_from, int64_t allow_token,
+                                 const uint16_t* history, int64_t hist_len,
+                                 q3s_transfer_callback observer, void* observer_user_data,
+                                 uint32_t* token, int32_t* row_status, void* stream);
+/* Sampler::sample / sample_with_transfer_observer (sampling.rs:183-221):
+ * do_sample = temperature > 0. */
+int q3s_sampler_sample(q3s_sampler* s, const void* logits, int32_t dtype, int64_t n,
+                       const q3s_sampling_options* options, int64_t suppress_from,
+                       int64_t allow_token, const uint16_t* history, int64_t hist_len,
+                       uint32_t* token, int32_t* row_status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* Q3S_SAMPLER_H */
