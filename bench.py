@@ -1,0 +1,448 @@
+#!/usr/bin/env python3
+"""Benchmark of the fused token-sampling path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload (per GPU, weak scaling): the bandwidth configuration, 65536 rows x
+3072 f32 logits ~ N(0, 1), top_k 50, top_p 1.0, temperature 1.0, no penalty;
+one step = one fused sampling launch over the 65536 rows.  The logits (805 MB)
+exceed the 126 MB L2, so consecutive steps stream them from HBM.
+
+`value` is whole-job rows/s with the inputs resident in HBM.  `e2e` is the same
+metric through the C ABI with host buffers: each step copies the logits and
+the per-row seeds from pinned host memory and the tokens and status bytes
+back.  `--impl reference` times the CPU restatement of the reference sampler
+(src/talker/sampling.rs, with glibc expf as Rust's f32::exp uses on Linux) on
+the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "qwen3tts-rs_b200"))
+
+METRIC = "sampled rows/sec at vocab 3072, B=1024 and 65536 (1/2/4/8 B200); % HBM roofline"
+ROWS = 65536
+VOCAB = 3072
+TOP_K = 50
+# Algorithmic bytes per row of the bandwidth workload: 3072 f32 logits,
+# the Philox seed and subsequence (8 + 8), the token (4) and the status (1).
+BYTES_PER_ROW = 4 * VOCAB + 16 + 4 + 1
+# DRAM bytes per launch of the sampling kernel from the ncu capture summarised
+# in profiles/sample_kernel_bandwidth_65536x3072.md (None until captured).
+NCU_TRAFFIC_PER_LAUNCH = None
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peak_gbs():
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        "hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+        "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.01):
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._h = None
+        self.period = period_s
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._h = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                util = nv.nvmlDeviceGetUtilizationRates(self._h).gpu
+                self.samples.append((mhz, reasons, util))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._h is not None:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [],
+                    "samples": 0}
+        mhz = [s[0] for s in self.samples]
+        active = 0
+        for s in self.samples:
+            active |= s[1]
+        reasons = [name for name, bit in self.REASONS.items() if active & bit]
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def oracle_mod():
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle  # CPU baseline / reference arm only
+    return oracle
+
+
+def cpu_rows_per_s(oracle, logits, vocab, params, target_s: float, threads: int):
+    """Times the CPU restatement (glibc expf) over a sample of rows."""
+    import numpy as np
+    R = logits.shape[0]
+    flat = np.ascontiguousarray(logits.reshape(-1))
+    off = np.arange(R, dtype=np.int64) * vocab
+    voc = np.full(R, vocab, np.int32)
+    seeds = np.arange(R, dtype=np.uint64)
+    sub = np.zeros(R, np.uint64)
+    # Size the sample from a short probe.
+    probe = min(R, max(64, 16 * threads))
+    t0 = time.perf_counter()
+    oracle.sample_rows(flat, off[:probe], voc[:probe], params, seeds[:probe], sub[:probe],
+                       exp_mode=oracle.EXP_LIBM, nthreads=threads)
+    rate = probe / max(time.perf_counter() - t0, 1e-6)
+    n = int(min(R, max(probe, rate * target_s)))
+    t0 = time.perf_counter()
+    oracle.sample_rows(flat, off[:n], voc[:n], params, seeds[:n], sub[:n],
+                       exp_mode=oracle.EXP_LIBM, nthreads=threads)
+    dt = time.perf_counter() - t0
+    return n / dt, n
+
+
+def run_reference(args, world, rank):
+    """CPU arm: the restated reference sampler on every host thread."""
+    import numpy as np
+    if rank != 0:
+        return 0
+    oracle = oracle_mod()
+    import q3s
+    threads = cpu_threads()
+    rng = np.random.default_rng(3)
+    sample = 8192
+    logits = rng.standard_normal((sample, VOCAB), dtype=np.float32)
+    params = q3s.make_params(1, top_k=TOP_K, top_p=1.0, temperature=1.0)
+    flat = logits.reshape(-1)
+    off = np.arange(sample, dtype=np.int64) * VOCAB
+    voc = np.full(sample, VOCAB, np.int32)
+    seeds = np.arange(sample, dtype=np.uint64)
+    sub = np.zeros(sample, np.uint64)
+    # Rows per step: about 50 ms of work so K + W steps end within minutes.
+    t0 = time.perf_counter()
+    oracle.sample_rows(flat, off[:256], voc[:256], params, seeds[:256], sub[:256],
+                       exp_mode=oracle.EXP_LIBM, nthreads=threads)
+    rate = 256 / max(time.perf_counter() - t0, 1e-6)
+    per_step = int(min(sample, max(256, rate * 0.05)))
+
+    def step(i):
+        s = (i * per_step) % (sample - per_step + 1)
+        oracle.sample_rows(flat, off[s:s + per_step], voc[s:s + per_step], params,
+                           seeds[s:s + per_step], sub[s:s + per_step],
+                           exp_mode=oracle.EXP_LIBM, nthreads=threads)
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(i)
+    dt = time.perf_counter() - t0
+    value = per_step * args.steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3 / max(args.steps, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(),
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port",
+                         "sample": f"{per_step} rows of 3072 f32 N(0,1) per step, k=50, "
+                                   f"CPU restatement of src/talker/sampling.rs with glibc expf"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config():
+    return {"workload": "bandwidth: 65536 rows x 3072 f32 logits ~N(0,1) per GPU, top_k 50, "
+                        "top_p 1.0, temperature 1.0, no penalty",
+            "rows_per_gpu": ROWS, "vocab": VOCAB, "top_k": TOP_K, "global_batch": None,
+            "l2": "inputs 805 MB per step > 126 MB L2 (no flush needed)",
+            "parallelism": "row shards, no collective"}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    args = ap.parse_args()
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import q3s
+    from q3s import workloads
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ctx = q3s.Context(local)
+    w = workloads.bandwidth(dev, rows=ROWS, top_k=TOP_K, seed=3 + rank)
+    a = w.device_args(dev)
+    params, seeds, subseqs = a["params"], a["seeds"], a["subseqs"]
+    tokens = torch.empty(ROWS, dtype=torch.int32, device=dev)
+    status = torch.empty(ROWS, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def launch():
+        q3s.sample_batch(w.logits, params, seeds, subseqs, ctx=ctx, out=(tokens, status))
+
+    for _ in range(max(args.warmup, 3)):
+        launch()
+    torch.cuda.synchronize()
+    if not bool((status == 0).all()):
+        raise RuntimeError("sampling failed on the benchmark workload")
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    t_begin = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        t_begin.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            launch()
+            ends[i].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    elapsed_ms = max_over_ranks(t_begin.elapsed_time(t_end))
+    kernel_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / max(args.steps, 1)
+    kernel_ms = max_over_ranks(kernel_ms)
+    value = world * ROWS * args.steps / (elapsed_ms / 1e3)
+    peak, peak_kind = measured_peak_gbs()
+    achieved = ROWS * BYTES_PER_ROW / (kernel_ms / 1e3) / 1e9
+
+    # End to end through the C ABI with host buffers.
+    e2e = None
+    if args.e2e_steps > 0:
+        host_logits = torch.empty((ROWS, VOCAB), dtype=torch.float32, pin_memory=True)
+        host_logits.copy_(w.logits)
+        host_seeds = seeds.cpu().pin_memory()
+        host_sub = subseqs.cpu().pin_memory()
+        host_tok = torch.empty(ROWS, dtype=torch.int32, pin_memory=True)
+        host_st = torch.empty(ROWS, dtype=torch.uint8, pin_memory=True)
+        dev_logits = torch.empty_like(w.logits)
+        dev_seeds = torch.empty_like(seeds)
+        dev_sub = torch.empty_like(subseqs)
+        chunks = 8
+        cr = ROWS // chunks
+        streams = [torch.cuda.Stream(dev) for _ in range(2)]
+
+        def e2e_step():
+            ev0 = torch.cuda.Event()
+            ev0.record(stream)
+            for c in range(chunks):
+                s = streams[c % 2]
+                s.wait_event(ev0)
+                with torch.cuda.stream(s):
+                    sl = slice(c * cr, (c + 1) * cr)
+                    dev_logits[sl].copy_(host_logits[sl], non_blocking=True)
+                    dev_seeds[sl].copy_(host_seeds[sl], non_blocking=True)
+                    dev_sub[sl].copy_(host_sub[sl], non_blocking=True)
+                    q3s.sample_batch(dev_logits[sl], params, dev_seeds[sl], dev_sub[sl],
+                                     ctx=ctx, stream=s.cuda_stream,
+                                     out=(tokens[sl], status[sl]))
+                    host_tok[sl].copy_(tokens[sl], non_blocking=True)
+                    host_st[sl].copy_(status[sl], non_blocking=True)
+            for s in streams:
+                stream.wait_stream(s)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.e2e_steps
+        if not bool((host_st == 0).all()):
+            raise RuntimeError("end-to-end sampling failed")
+        e2e = {"value": world * ROWS / (e2e_ms / 1e3), "unit": "rows/s",
+               "h2d_bytes_per_step": ROWS * (4 * VOCAB + 16),
+               "d2h_bytes_per_step": ROWS * 5, "ms_per_step": e2e_ms}
+        del host_logits, dev_logits
+
+    results = {}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_secondary:
+        results = secondary(ctx, dev, q3s, workloads, np, torch)
+        oracle = oracle_mod()
+        sample_rows = 16384
+        x = w.logits[:sample_rows].cpu().numpy()
+        threads = cpu_threads()
+        rate, n = cpu_rows_per_s(oracle, x, VOCAB, q3s.make_params(1, top_k=TOP_K), 10.0,
+                                 threads)
+        cpu = {"value": rate, "unit": "rows/s", "cores": threads, "kind": "port",
+               "sample": f"{n} rows of the bandwidth workload (k=50), CPU restatement of "
+                         f"src/talker/sampling.rs with glibc expf, {threads} threads"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": dict(workload_config(), global_batch=ROWS * world),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": NCU_TRAFFIC_PER_LAUNCH,
+                         "bytes_per_row": BYTES_PER_ROW, "kernel_ms": kernel_ms},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(),
+            "results": results,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def secondary(ctx, dev, q3s, workloads, np, torch):
+    """Other configurations, device-resident, timed with CUDA events."""
+    out = {}
+
+    def time_launches(fn, iters):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters
+
+    # B=1024 talker batch (penalty over histories, suppression, top-p 0.8).
+    wb = workloads.talker_batch(dev, rows=1024)
+    ab = wb.device_args(dev)
+    pb, sb, ub = ab.pop("params"), ab.pop("seeds"), ab.pop("subseqs")
+    ms = time_launches(lambda: q3s.sample_batch(wb.logits, pb, sb, ub, ctx=ctx, **ab), 50)
+    hist_bytes = int(wb.history_offsets[-1]) * 2
+    out["talker_batch_1024"] = {
+        "rows_per_s": 1024 / (ms / 1e3), "ms_per_launch": ms,
+        "gbs": (1024 * (4 * 3072 + 16 + 8 + 5) + hist_bytes) / (ms / 1e3) / 1e9}
+    for k in (1, 256):
+        wk = workloads.bandwidth(dev, rows=65536, top_k=k, seed=9)
+        ak = wk.device_args(dev)
+        pk, sk, uk = ak.pop("params"), ak.pop("seeds"), ak.pop("subseqs")
+        ms = time_launches(lambda: q3s.sample_batch(wk.logits, pk, sk, uk, ctx=ctx), 50)
+        out[f"bandwidth_k{k}"] = {"rows_per_s": 65536 / (ms / 1e3), "ms_per_launch": ms,
+                                  "gbs": 65536 * BYTES_PER_ROW / (ms / 1e3) / 1e9}
+        del wk
+    # Code-predictor frame: 15 dependent bf16 [64, 2048] launches.
+    wc = workloads.cp_frame(dev)
+    ac = wc.device_args(dev)
+    pc = ac.pop("params")
+    sc, uc = ac.pop("seeds"), ac.pop("subseqs")
+    x = wc.logits.view(15, 64, 2048)
+
+    def frame():
+        for g in range(15):
+            q3s.sample_batch(x[g], pc, sc[g * 64:(g + 1) * 64], uc[g * 64:(g + 1) * 64], ctx=ctx)
+    ms = time_launches(frame, 20)
+    out["cp_frame_64x15"] = {"us_per_group": ms * 1e3 / 15, "rows_per_s": 960 / (ms / 1e3)}
+    # Single-stream talker step through the stateful Sampler (host round trip).
+    ws = workloads.talker_single(dev, steps=200)
+    s = q3s.Sampler(42, ctx)
+    o = q3s.SamplingOptions(0.9, 50, 1.0, 1.05)
+    hist = list(ws.history[:256])
+    for i in range(5):
+        s.sample_with_mode(ws.logits[i], o, True, 2048, 2150, hist)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(200):
+        s.sample_with_mode(ws.logits[i], o, True, 2048, 2150, hist)
+    dt = time.perf_counter() - t0
+    out["talker_single_step"] = {"us_per_step": dt * 1e6 / 200,
+                                 "note": "stateful Sampler call incl. H2D params/history and "
+                                         "D2H token+status, host wall clock"}
+    return out
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -185,7 +185,7 @@ void q3s_sampler_destroy(q3s_sampler* s);
 uint64_t q3s_sampler_subsequence_counter(const q3s_sampler* s);
 void q3s_sampler_set_subsequence_counter(q3s_sampler* s, uint64_t subseq);
 /* Sampler::diagnostics (sampling.rs:179). */
-int q3s_sampler_diagnostics(const q3s_sampler* s, q3s_sampler_diagnostics* out);
+int q3s_sampler_get_diagnostics(const q3s_sampler* s, q3s_sampler_diagnostics* out);
 
 /* Sampler::sample_with_mode_and_transfer_observer (sampling.rs:247-334).
  * logits: device pointer to n elements of dtype.  history: HOST pointer to

@@ -72,24 +72,25 @@ extern "C" float q3o_cr_expf(float xf) {
   if (xf != xf) return xf + xf;
   if (xf < -104.0f) return 0.0f;  // exp(-104) < 2^-150: rounds to +0
   if (xf > 89.0f) return INFINITY;  // exp(89) > FLT_MAX
-  const double INV_LN2 = 1.4426950408889634;          // 1/ln2 rounded
-  const double LN2_HI = 6.9314718055994529e-01;       // ln2 rounded to binary64
-  const double LN2_LO = 2.3190468138462996e-17;       // ln2 - LN2_HI
+  const double INV_LN2 = 0x1.71547652b82fep+0;  // 1/ln2 rounded to binary64
+  const double LN2_HI = 0x1.62e42fefa39efp-1;   // ln2 rounded to binary64
+  const double LN2_LO = 0x1.abc9e3b39803fp-56;  // ln2 - LN2_HI rounded
   double x = (double)xf;
   double kd = nearbyint(x * INV_LN2);
   double r = fma(-kd, LN2_HI, x);
   r = fma(-kd, LN2_LO, r);
-  double p = 1.0 / 6227020800.0;           // 1/13!
-  p = fma(p, r, 1.0 / 479001600.0);        // 1/12!
-  p = fma(p, r, 1.0 / 39916800.0);         // 1/11!
-  p = fma(p, r, 1.0 / 3628800.0);          // 1/10!
-  p = fma(p, r, 1.0 / 362880.0);           // 1/9!
-  p = fma(p, r, 1.0 / 40320.0);            // 1/8!
-  p = fma(p, r, 1.0 / 5040.0);             // 1/7!
-  p = fma(p, r, 1.0 / 720.0);              // 1/6!
-  p = fma(p, r, 1.0 / 120.0);              // 1/5!
-  p = fma(p, r, 1.0 / 24.0);               // 1/4!
-  p = fma(p, r, 1.0 / 6.0);                // 1/3!
+  // Taylor coefficients 1/n!, each the binary64 nearest to the exact value.
+  double p = 0x1.6124613a86d09p-33;        // 1/13!
+  p = fma(p, r, 0x1.1eed8eff8d898p-29);    // 1/12!
+  p = fma(p, r, 0x1.ae64567f544e4p-26);    // 1/11!
+  p = fma(p, r, 0x1.27e4fb7789f5cp-22);    // 1/10!
+  p = fma(p, r, 0x1.71de3a556c734p-19);    // 1/9!
+  p = fma(p, r, 0x1.a01a01a01a01ap-16);    // 1/8!
+  p = fma(p, r, 0x1.a01a01a01a01ap-13);    // 1/7!
+  p = fma(p, r, 0x1.6c16c16c16c17p-10);    // 1/6!
+  p = fma(p, r, 0x1.1111111111111p-7);     // 1/5!
+  p = fma(p, r, 0x1.5555555555555p-5);     // 1/4!
+  p = fma(p, r, 0x1.5555555555555p-3);     // 1/3!
   p = fma(p, r, 0.5);                      // 1/2!
   p = fma(p, r, 1.0);
   p = fma(p, r, 1.0);

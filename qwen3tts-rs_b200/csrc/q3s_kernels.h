@@ -1,0 +1,44 @@
+// Internal interface between the C ABI (q3s_capi.cpp) and the kernels
+// (q3s_sample.cu).  Not installed; callers use include/q3s_sampler.h.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+#include "../../include/q3s_sampler.h"
+
+namespace q3s {
+
+struct KernelArgs {
+  const void* logits;
+  int dtype;
+  int vocab;  // every row's vocabulary, or an upper bound when row_vocab is set
+  long long num_rows;
+  long long row_stride;
+  const long long* row_offsets;
+  const int* row_vocab;
+  const q3s_row_params* params;
+  long long params_stride;
+  const unsigned long long* seeds;
+  const unsigned long long* subseqs;
+  const unsigned short* history;
+  const long long* history_offsets;
+  unsigned* tokens;
+  unsigned char* status;
+  const float* uniform_override;
+  float* probs;
+  unsigned char* masks;
+  long long probs_stride;
+  int vcap;  // per-warp row capacity in elements (multiple of 32)
+};
+
+size_t sample_smem_per_warp(int vcap);
+int sample_max_warps(int vcap, size_t smem_limit);
+cudaError_t launch_sample(const KernelArgs& a, int grid, int warps, cudaStream_t stream);
+cudaError_t launch_greedy(const void* logits, int dtype, long long num_rows, long long row_stride,
+                          int n, long long sf, long long allow, int mode, uint32_t* tokens,
+                          uint8_t* status, int grid, cudaStream_t stream);
+
+}  // namespace q3s

@@ -1,0 +1,453 @@
+"""Python binding of the B200 sampler C ABI (include/q3s_sampler.h).
+
+The product path is the CUDA library lib/libq3s_sampler.so; this module only
+marshals arguments through ctypes.  Loading fails loudly when the library is
+missing: there is no CPU fallback.
+
+Surface mirrored from the reference (qwen3tts-rs src/talker/sampling.rs):
+    SamplingOptions            sampling.rs:19-25, greedy() :133-142
+    Sampler                    sampling.rs:144-335 (sample, sample_with_mode,
+                               sample_with_transfer_observer,
+                               sample_with_mode_and_transfer_observer,
+                               subsequence_counter, diagnostics)
+    greedy_select_on_device    sampling.rs:72-117
+    greedy_select              sampling.rs:40-60 (on device, many rows)
+plus the batched entry point `sample_batch`, one fused launch over many rows.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+from pathlib import Path
+from typing import Callable, Optional, Sequence
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parent.parent
+LIB_PATH = PKG / "lib" / "libq3s_sampler.so"
+
+OK = 0
+E_INVALID_ARGUMENT = -1
+E_CUDA = -2
+E_NO_DEVICE = -3
+E_OUT_OF_MEMORY = -4
+E_SAMPLING = -5
+
+STATUS_OK = 0
+STATUS_INVALID_REPETITION_PENALTY = 1
+STATUS_INVALID_TEMPERATURE = 2
+STATUS_INVALID_TOP_P = 3
+STATUS_SUPPRESSION_NO_CANDIDATE = 4
+STATUS_NO_CANDIDATE = 5
+STATUS_INVALID_DENOMINATOR = 6
+STATUS_UNSUPPORTED = 7
+MAX_VOCAB = 4096
+
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+NONE = -1
+GREEDY_SELECT = 0
+GREEDY_ON_DEVICE = 1
+TRANSFER_SAMPLED_TOKEN = 0
+
+# q3s_row_params (48 bytes).
+ROW_PARAMS_DTYPE = np.dtype([
+    ("temperature", "<f8"), ("top_p", "<f8"), ("repetition_penalty", "<f8"),
+    ("top_k", "<u4"), ("do_sample", "<u4"), ("suppress_from", "<i4"),
+    ("allow_token", "<i4"), ("ctr_lo", "<u4"), ("reserved", "<u4"),
+])
+assert ROW_PARAMS_DTYPE.itemsize == 48
+
+
+class SamplingError(RuntimeError):
+    """A sampling call failed; `status` is the Q3S_STATUS_* of the row."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+class LibraryError(RuntimeError):
+    pass
+
+
+class _Options(ctypes.Structure):
+    _fields_ = [("temperature", ctypes.c_double), ("top_k", ctypes.c_uint64),
+                ("top_p", ctypes.c_double), ("repetition_penalty", ctypes.c_double)]
+
+
+class _Batch(ctypes.Structure):
+    _fields_ = [
+        ("logits", ctypes.c_void_p), ("dtype", ctypes.c_int32), ("vocab", ctypes.c_int32),
+        ("num_rows", ctypes.c_int64), ("row_stride", ctypes.c_int64),
+        ("row_offsets", ctypes.c_void_p), ("row_vocab", ctypes.c_void_p),
+        ("params", ctypes.c_void_p), ("params_stride", ctypes.c_int64),
+        ("seeds", ctypes.c_void_p), ("subseqs", ctypes.c_void_p),
+        ("history", ctypes.c_void_p), ("history_offsets", ctypes.c_void_p),
+        ("tokens", ctypes.c_void_p), ("status", ctypes.c_void_p),
+        ("uniform_override", ctypes.c_void_p), ("probs", ctypes.c_void_p),
+        ("masks", ctypes.c_void_p), ("probs_stride", ctypes.c_int64),
+    ]
+
+
+class _Diagnostics(ctypes.Structure):
+    _fields_ = [("call_count", ctypes.c_uint32), ("sampled_calls", ctypes.c_uint32),
+                ("greedy_calls", ctypes.c_uint32), ("history_nonempty_calls", ctypes.c_uint32),
+                ("history_nonempty_sequence", ctypes.c_uint8 * 64),
+                ("sequence", ctypes.c_uint8 * 64), ("sequence_len", ctypes.c_uint64)]
+
+
+TRANSFER_CALLBACK = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                     ctypes.c_uint64)
+
+# Every symbol include/q3s_sampler.h declares.
+EXPORTED_SYMBOLS = (
+    "q3s_abi_version", "q3s_last_error", "q3s_status_message", "q3s_context_create",
+    "q3s_context_destroy", "q3s_sample_batch", "q3s_greedy_batch", "q3s_sampler_create",
+    "q3s_sampler_destroy", "q3s_sampler_subsequence_counter",
+    "q3s_sampler_set_subsequence_counter", "q3s_sampler_get_diagnostics",
+    "q3s_sampler_sample_with_mode", "q3s_sampler_sample",
+)
+
+_lib = None
+
+
+def load(path: Optional[os.PathLike] = None):
+    """Loads the CUDA sampler library (building it first when nvcc is here)."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path is not None else LIB_PATH
+    if not p.exists():
+        import importlib.util
+        spec = importlib.util.spec_from_file_location("_q3s_build", PKG / "build.py")
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        try:
+            mod.build()
+        except Exception as exc:  # no toolkit: fail loudly, never fall back
+            raise LibraryError(f"sampler library missing at {p} and it cannot be built: {exc}")
+    L = ctypes.CDLL(str(p))
+    L.q3s_abi_version.restype = ctypes.c_int
+    L.q3s_last_error.restype = ctypes.c_char_p
+    L.q3s_status_message.restype = ctypes.c_char_p
+    L.q3s_status_message.argtypes = [ctypes.c_int]
+    L.q3s_context_create.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]
+    L.q3s_context_destroy.argtypes = [ctypes.c_void_p]
+    L.q3s_context_destroy.restype = None
+    L.q3s_sample_batch.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Batch), ctypes.c_void_p]
+    L.q3s_greedy_batch.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                   ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                   ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    L.q3s_sampler_create.argtypes = [ctypes.c_void_p, ctypes.c_uint64,
+                                     ctypes.POINTER(ctypes.c_void_p)]
+    L.q3s_sampler_destroy.argtypes = [ctypes.c_void_p]
+    L.q3s_sampler_destroy.restype = None
+    L.q3s_sampler_subsequence_counter.argtypes = [ctypes.c_void_p]
+    L.q3s_sampler_subsequence_counter.restype = ctypes.c_uint64
+    L.q3s_sampler_set_subsequence_counter.argtypes = [ctypes.c_void_p, ctypes.c_uint64]
+    L.q3s_sampler_set_subsequence_counter.restype = None
+    L.q3s_sampler_get_diagnostics.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Diagnostics)]
+    L.q3s_sampler_sample_with_mode.argtypes = [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
+        ctypes.POINTER(_Options), ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_void_p, ctypes.c_int64, TRANSFER_CALLBACK, ctypes.c_void_p,
+        ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_int32), ctypes.c_void_p]
+    L.q3s_sampler_sample.argtypes = [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
+        ctypes.POINTER(_Options), ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+        ctypes.c_int64, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_int32),
+        ctypes.c_void_p]
+    if path is None:
+        _lib = L
+    return L
+
+
+def last_error() -> str:
+    return load().q3s_last_error().decode()
+
+
+def status_message(status: int) -> str:
+    return load().q3s_status_message(int(status)).decode()
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != OK:
+        raise LibraryError(f"{what} failed ({rc}): {last_error()}")
+
+
+@dataclass(frozen=True)
+class SamplingOptions:
+    """SamplingOptions (sampling.rs:19-25)."""
+    temperature: float
+    top_k: int
+    top_p: float
+    repetition_penalty: float
+
+    @staticmethod
+    def greedy() -> "SamplingOptions":
+        return SamplingOptions(0.0, 0, 1.0, 1.0)
+
+    def _c(self) -> _Options:
+        return _Options(float(self.temperature), int(self.top_k), float(self.top_p),
+                        float(self.repetition_penalty))
+
+
+def _none(v) -> int:
+    return NONE if v is None else int(v)
+
+
+class Context:
+    """A q3s_context on one device (one per device and host thread)."""
+
+    def __init__(self, device: int = 0):
+        self.device = int(device)
+        self._h = ctypes.c_void_p()
+        _check(load().q3s_context_create(self.device, ctypes.byref(self._h)),
+               "q3s_context_create")
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._h
+
+    def close(self) -> None:
+        if self._h:
+            load().q3s_context_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):  # pragma: no cover - interpreter shutdown order
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_default_ctx: dict = {}
+
+
+def default_context(device: Optional[int] = None) -> Context:
+    import torch
+    d = torch.cuda.current_device() if device is None else int(device)
+    if d not in _default_ctx:
+        _default_ctx[d] = Context(d)
+    return _default_ctx[d]
+
+
+def make_params(n: int = 1, **fields) -> np.ndarray:
+    """A q3s_row_params array; unspecified fields default to greedy-safe values."""
+    p = np.zeros(n, dtype=ROW_PARAMS_DTYPE)
+    p["temperature"] = 1.0
+    p["top_p"] = 1.0
+    p["repetition_penalty"] = 1.0
+    p["suppress_from"] = NONE
+    p["allow_token"] = NONE
+    p["do_sample"] = 1
+    for k, v in fields.items():
+        p[k] = v
+    return p
+
+
+def _dptr(t) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def sample_batch(logits, params, seeds=None, subseqs=None, *, row_offsets=None, row_vocab=None,
+                 vocab: Optional[int] = None, history=None, history_offsets=None,
+                 uniform_override=None, debug: bool = False, ctx: Optional[Context] = None,
+                 stream=None, out=None):
+    """One fused sampling launch over many rows (q3s_sample_batch).
+
+    logits: CUDA tensor, float32 or bfloat16, either [R, V] (row stride taken
+    from the tensor) or 1-D with row_offsets [R] (int64) and row_vocab [R]
+    (int32).  params: CUDA uint8 tensor holding R (or 1, broadcast)
+    q3s_row_params, or a numpy ROW_PARAMS_DTYPE array (copied to the device).
+    seeds / subseqs: CUDA int64 tensors [R] (the u64 bit patterns).
+    history: CUDA int16/uint16 tensor of concatenated ids with
+    history_offsets [R+1] int64.  Returns (tokens int32 [R], status uint8 [R])
+    and, with debug=True, also (probs [R, V] float32, masks [R, V] uint8).
+    """
+    import torch
+    dev = logits.device
+    if logits.dtype == torch.float32:
+        dt = DTYPE_F32
+    elif logits.dtype == torch.bfloat16:
+        dt = DTYPE_BF16
+    else:
+        raise TypeError("logits must be float32 or bfloat16")
+    if logits.dim() == 2:
+        R, V = logits.shape
+        stride = logits.stride(0)
+        if logits.stride(1) != 1:
+            raise ValueError("logits rows must be contiguous")
+    else:
+        if row_offsets is None:
+            raise ValueError("1-D logits need row_offsets")
+        R = row_offsets.numel()
+        stride = 0
+        V = int(vocab if vocab is not None else int(row_vocab.max()))
+    if vocab is not None:
+        V = int(vocab)
+    if isinstance(params, np.ndarray):
+        params = torch.from_numpy(params.view(np.uint8).copy()).to(dev)
+    nparams = params.numel() // ROW_PARAMS_DTYPE.itemsize
+    if nparams not in (1, R):
+        raise ValueError("params must hold 1 or R records")
+    ctx = ctx or default_context(dev.index)
+    if out is None:
+        tokens = torch.empty(R, dtype=torch.int32, device=dev)
+        status = torch.empty(R, dtype=torch.uint8, device=dev)
+    else:
+        tokens, status = out
+    probs = masks = None
+    if debug:
+        probs = torch.empty((R, V), dtype=torch.float32, device=dev)
+        masks = torch.empty((R, V), dtype=torch.uint8, device=dev)
+    b = _Batch()
+    b.logits = logits.data_ptr()
+    b.dtype = dt
+    b.vocab = V
+    b.num_rows = R
+    b.row_stride = stride
+    b.row_offsets = _dptr(row_offsets)
+    b.row_vocab = _dptr(row_vocab)
+    b.params = params.data_ptr()
+    b.params_stride = 0 if nparams == 1 else 1
+    b.seeds = _dptr(seeds)
+    b.subseqs = _dptr(subseqs)
+    b.history = _dptr(history)
+    b.history_offsets = _dptr(history_offsets)
+    b.tokens = tokens.data_ptr()
+    b.status = status.data_ptr()
+    b.uniform_override = _dptr(uniform_override)
+    b.probs = _dptr(probs)
+    b.masks = _dptr(masks)
+    b.probs_stride = V if debug else 0
+    s = torch.cuda.current_stream(dev).cuda_stream if stream is None else stream
+    _check(load().q3s_sample_batch(ctx.handle, ctypes.byref(b), ctypes.c_void_p(s)),
+           "q3s_sample_batch")
+    if debug:
+        return tokens, status, probs, masks
+    return tokens, status
+
+
+def greedy_batch(logits, suppress_from=None, allow_token=None, mode: int = GREEDY_SELECT,
+                 ctx: Optional[Context] = None, stream=None):
+    """Greedy argmax rows on device (q3s_greedy_batch); logits [R, V] CUDA."""
+    import torch
+    if logits.dim() == 1:
+        logits = logits.view(1, -1)
+    R, V = logits.shape
+    dt = DTYPE_F32 if logits.dtype == torch.float32 else DTYPE_BF16
+    ctx = ctx or default_context(logits.device.index)
+    tokens = torch.empty(R, dtype=torch.int32, device=logits.device)
+    status = torch.empty(R, dtype=torch.uint8, device=logits.device)
+    s = torch.cuda.current_stream(logits.device).cuda_stream if stream is None else stream
+    _check(load().q3s_greedy_batch(ctx.handle, ctypes.c_void_p(logits.data_ptr()), dt, R,
+                                   logits.stride(0), V, _none(suppress_from), _none(allow_token),
+                                   mode, ctypes.c_void_p(tokens.data_ptr()),
+                                   ctypes.c_void_p(status.data_ptr()), ctypes.c_void_p(s)),
+           "q3s_greedy_batch")
+    return tokens, status
+
+
+def greedy_select_on_device(logits, suppress_from=None, allow_token=None):
+    """greedy_select_on_device (sampling.rs:72-117): a [1, 1] int32 device
+    tensor; its value equals the vocabulary size when nothing is finite."""
+    if logits.dim() == 2 and logits.shape[0] != 1:
+        raise ValueError("greedy selection requires batch=1")
+    if logits.numel() == 0:
+        raise ValueError("greedy selection requires a non-empty vocabulary")
+    tokens, _ = greedy_batch(logits.reshape(1, -1), suppress_from, allow_token, GREEDY_ON_DEVICE)
+    return tokens.view(1, 1)
+
+
+def greedy_select(logits, suppress_from=None, allow_token=None) -> int:
+    """greedy_select (sampling.rs:40-60) on device; raises SamplingError."""
+    tokens, status = greedy_batch(logits.reshape(1, -1), suppress_from, allow_token,
+                                  GREEDY_SELECT)
+    st = int(status.item())
+    if st != STATUS_OK:
+        raise SamplingError(st, status_message(st))
+    return int(tokens.item())
+
+
+class Sampler:
+    """Sampler (sampling.rs:144-335) on the device: one Philox stream whose
+    subsequence counter advances once per sampled call that drew."""
+
+    def __init__(self, seed: int, ctx: Optional[Context] = None):
+        self._ctx = ctx or default_context()
+        self._h = ctypes.c_void_p()
+        _check(load().q3s_sampler_create(self._ctx.handle, int(seed) & (2**64 - 1),
+                                         ctypes.byref(self._h)), "q3s_sampler_create")
+
+    def __del__(self):  # pragma: no cover
+        try:
+            if self._h:
+                load().q3s_sampler_destroy(self._h)
+        except Exception:
+            pass
+
+    def subsequence_counter(self) -> int:
+        return int(load().q3s_sampler_subsequence_counter(self._h))
+
+    def set_subsequence_counter(self, value: int) -> None:
+        load().q3s_sampler_set_subsequence_counter(self._h, int(value) & (2**64 - 1))
+
+    def diagnostics(self) -> dict:
+        d = _Diagnostics()
+        _check(load().q3s_sampler_get_diagnostics(self._h, ctypes.byref(d)),
+               "q3s_sampler_get_diagnostics")
+        n = int(d.sequence_len)
+        return {"call_count": d.call_count, "sampled_calls": d.sampled_calls,
+                "greedy_calls": d.greedy_calls,
+                "history_nonempty_calls": d.history_nonempty_calls, "sequence_len": n,
+                "sequence": list(d.sequence)[:n],
+                "history_nonempty_sequence": list(d.history_nonempty_sequence)[:n]}
+
+    def sample_with_mode_and_transfer_observer(
+            self, logits, options: SamplingOptions, do_sample: bool, suppress_from=None,
+            allow_token=None, history: Sequence[int] = (),
+            observer: Optional[Callable[[int, int, int], None]] = None, stream=None) -> int:
+        import torch
+        if not logits.is_cuda:
+            raise ValueError("logits must be a CUDA tensor")
+        x = logits.reshape(-1)
+        if not x.is_contiguous():
+            x = x.contiguous()
+        dt = DTYPE_F32 if x.dtype == torch.float32 else DTYPE_BF16
+        if x.dtype not in (torch.float32, torch.bfloat16):
+            raise TypeError("logits must be float32 or bfloat16")
+        h = np.ascontiguousarray(np.asarray(history, dtype=np.uint16))
+        tok = ctypes.c_uint32(0)
+        st = ctypes.c_int32(0)
+        cb = TRANSFER_CALLBACK(0)
+        if observer is not None:
+            cb = TRANSFER_CALLBACK(lambda _u, direction, event, n: observer(direction, event, n))
+        s = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
+        rc = load().q3s_sampler_sample_with_mode(
+            self._h, ctypes.c_void_p(x.data_ptr() if x.numel() else 0), dt, x.numel(),
+            ctypes.byref(options._c()), 1 if do_sample else 0, _none(suppress_from),
+            _none(allow_token), h.ctypes.data_as(ctypes.c_void_p) if h.size else None, h.size,
+            cb, None, ctypes.byref(tok), ctypes.byref(st), ctypes.c_void_p(s))
+        if rc == E_SAMPLING:
+            raise SamplingError(st.value, status_message(st.value))
+        _check(rc, "q3s_sampler_sample_with_mode")
+        return int(tok.value)
+
+    def sample_with_mode(self, logits, options, do_sample, suppress_from=None, allow_token=None,
+                         history=()) -> int:
+        return self.sample_with_mode_and_transfer_observer(logits, options, do_sample,
+                                                           suppress_from, allow_token, history)
+
+    def sample_with_transfer_observer(self, logits, options, suppress_from=None,
+                                      allow_token=None, history=(), observer=None) -> int:
+        return self.sample_with_mode_and_transfer_observer(
+            logits, options, options.temperature > 0.0, suppress_from, allow_token, history,
+            observer)
+
+    def sample(self, logits, options, suppress_from=None, allow_token=None, history=()) -> int:
+        return self.sample_with_mode(logits, options, options.temperature > 0.0, suppress_from,
+                                     allow_token, history)
