@@ -64,6 +64,9 @@ struct q3s_context {
   size_t hist_cap = 0;
   unsigned* h_out = nullptr;  // pinned: token, status byte in the next word
   unsigned* d_out = nullptr;
+  // General-path workspace of the sampling kernel (grown on demand).
+  unsigned char* scratch = nullptr;
+  size_t scratch_bytes = 0;
 };
 
 struct q3s_sampler {
@@ -141,6 +144,7 @@ void q3s_context_destroy(q3s_context* c) {
     if (c->d_hist) cudaFree(c->d_hist);
     if (c->h_out) cudaFreeHost(c->h_out);
     if (c->d_out) cudaFree(c->d_out);
+    if (c->scratch) cudaFree(c->scratch);
   }
   delete c;
 }
@@ -188,11 +192,23 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* b, void* stream) {
   a.probs_stride = b->probs_stride;
   int cap = b->vocab < Q3S_MAX_VOCAB ? b->vocab : Q3S_MAX_VOCAB;
   a.vcap = ((cap > 0 ? cap : 1) + 31) / 32 * 32;
-  const int warps = q3s::sample_max_warps(a.vcap, ctx->smem_optin);
+  const int warps = q3s::sample_max_warps(a.vcap, b->dtype, ctx->smem_optin);
   if (warps < 1) return fail(Q3S_E_INVALID_ARGUMENT, "vocabulary does not fit shared memory");
   long long blocks = (b->num_rows + warps - 1) / warps;
   if (blocks > ctx->sm_count) blocks = ctx->sm_count;
-  cudaError_t e = q3s::launch_sample(a, (int)blocks, warps, (cudaStream_t)stream);
+  const size_t need = (size_t)blocks * warps * q3s::sample_scratch_per_warp(a.vcap);
+  cudaError_t e;
+  if (need > ctx->scratch_bytes) {
+    // Launches on one context are stream-ordered users of this workspace.
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    ctx->scratch = nullptr;
+    ctx->scratch_bytes = 0;
+    if ((e = cudaMalloc((void**)&ctx->scratch, need)) != cudaSuccess)
+      return cuda_fail(e, "cudaMalloc(sampler workspace)");
+    ctx->scratch_bytes = need;
+  }
+  a.scratch = ctx->scratch;
+  e = q3s::launch_sample(a, (int)blocks, warps, (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "sample kernel launch");
   return Q3S_OK;
 }

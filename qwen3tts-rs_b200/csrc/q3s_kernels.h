@@ -32,10 +32,12 @@ struct KernelArgs {
   unsigned char* masks;
   long long probs_stride;
   int vcap;  // per-warp row capacity in elements (multiple of 32)
+  unsigned char* scratch;  // general-path workspace: sample_scratch_per_warp(vcap) per warp
 };
 
-size_t sample_smem_per_warp(int vcap);
-int sample_max_warps(int vcap, size_t smem_limit);
+size_t sample_smem_per_warp(int vcap, int dtype);
+size_t sample_scratch_per_warp(int vcap);
+int sample_max_warps(int vcap, int dtype, size_t smem_limit);
 cudaError_t launch_sample(const KernelArgs& a, int grid, int warps, cudaStream_t stream);
 cudaError_t launch_greedy(const void* logits, int dtype, long long num_rows, long long row_stride,
                           int n, long long sf, long long allow, int mode, uint32_t* tokens,

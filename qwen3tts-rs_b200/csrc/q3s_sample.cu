@@ -14,12 +14,27 @@
 // the draw's cumulative) is accumulated sequentially here too, over the same
 // non-zero terms in the same order.  Terms the reference adds that are exact
 // zeros (exp(-inf)) are skipped, which leaves an f32 sum unchanged.  The
-// parallel parts (max, counts, radix selection, sorting) are order-free.
+// parallel parts (max, counts, selection, sorting) are order-free.
 //
-// Layout: a persistent grid of warps strides over rows.  Each warp owns a
-// shared-memory workspace: the row as f32 (A), a compacted list of surviving
-// candidates in vocabulary order (B values, BI indices), a bitmap, a 256-bin
-// histogram and a 256-key sort buffer.
+// Data movement: a persistent grid of warps strides over rows.  Each warp
+// owns one shared-memory stage; its next row is fetched by a bulk copy (TMA,
+// cp.async.bulk, no multicast) that completes on the warp's mbarrier while the
+// warp finishes the current row.  The row is read from the stage once in the
+// common case (the "fast path"):
+//   1. one scan of the stage computes every 16-byte vector's maximum (kept in
+//      registers) and the row maximum;
+//   2. a threshold tau is chosen on the vector maxima so that at least k
+//      vectors (hence at least k elements) reach it: the candidates
+//      {x >= tau} then contain the whole top-k set, ties included;
+//   3. only the vectors whose maximum reaches tau are re-read to collect the
+//      candidates (a few hundred of the row's thousands of elements); the
+//      stage is then released to the next row's copy;
+//   4. the exact k-th largest candidate is found by radix selection, the
+//      survivors are put in vocabulary order through a bitmap, and the
+//      softmax / top-p / draw run on that short list.
+// Rows outside the fast path (top_k off or above 256, a temperature whose
+// reciprocal is 0 or infinite, a candidate overflow) run the same algorithm
+// on full-row lists kept in a per-warp global workspace ("general path").
 
 #include <cstdint>
 
@@ -30,77 +45,209 @@
 namespace q3s {
 namespace {
 
-constexpr int MAX_WARPS = 8;
+constexpr int MAX_WARPS = 12;
+constexpr int CAP = 512;   // fast-path candidate capacity per warp
+constexpr int LCAP = 512;  // fast-path survivor-list capacity per warp
+constexpr int FAST_MAX_K = 256;
+constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;  // bounded wait for a stage: 1 s
 
-struct WarpSpace {
-  float* A;                 // [vcap] the row: raw logits, then transformed values x
-  float* B;                 // [vcap] values of the candidate list
-  uint16_t* BI;             // [vcap] vocabulary indices of the candidate list
-  uint32_t* bm;             // [vcap/32] history bitmap
-  uint32_t* hist;           // [256]
-  unsigned long long* keys; // [256]
+template <int DT>
+struct Elem;
+template <>
+struct Elem<Q3S_DTYPE_F32> {
+  static constexpr int BYTES = 4, EPV = 4;
+};
+template <>
+struct Elem<Q3S_DTYPE_BF16> {
+  static constexpr int BYTES = 2, EPV = 8;
 };
 
 __host__ __device__ inline size_t align16(size_t b) { return (b + 15) & ~size_t(15); }
 
-__host__ __device__ inline size_t warp_space_bytes(int vcap) {
-  return align16(4u * vcap) * 2 + align16(2u * vcap) + align16(4u * (vcap / 32)) + 4u * 256 +
-         8u * 256;
+__host__ __device__ inline size_t stage_bytes(int vcap, int es) {
+  return align16((size_t)vcap * es + 16);
 }
 
-__device__ inline WarpSpace carve(unsigned char* base, int vcap) {
-  WarpSpace w;
+// Per-warp shared memory of the fast path.
+struct FastSpace {
+  unsigned char* stage;        // raw row, TMA destination
+  uint2* cand;                 // [CAP] (x bits, index); the nucleus sort aliases it
+  float* B;                    // [LCAP] softmax numerators of the survivor list
+  float* BX;                   // [LCAP] x of the survivor list
+  uint16_t* BI;                // [LCAP] vocabulary index of the survivor list
+  uint32_t* bm;                // [vcap/32] history bitmap, then survivor bitmap
+  uint16_t* wpre;              // [vcap/32] survivors before each bitmap word
+  uint32_t* hist;              // [256]
+  uint64_t* mbar;              // stage barrier
+  uint32_t* counter;           // candidate slot counter
+};
+
+__host__ __device__ inline size_t fast_bytes(int vcap, int es) {
+  return stage_bytes(vcap, es) + 8u * CAP + 4u * LCAP * 2 + align16(2u * LCAP) +
+         align16(4u * (vcap / 32)) + align16(2u * (vcap / 32)) + 4u * 256 + 16u;
+}
+
+__device__ inline FastSpace carve_fast(unsigned char* base, int vcap, int es) {
+  FastSpace f;
   size_t o = 0;
-  w.A = reinterpret_cast<float*>(base + o);
-  o += align16(4u * vcap);
-  w.B = reinterpret_cast<float*>(base + o);
-  o += align16(4u * vcap);
-  w.BI = reinterpret_cast<uint16_t*>(base + o);
-  o += align16(2u * vcap);
-  w.bm = reinterpret_cast<uint32_t*>(base + o);
+  f.stage = base;
+  o += stage_bytes(vcap, es);
+  f.cand = reinterpret_cast<uint2*>(base + o);
+  o += 8u * CAP;
+  f.B = reinterpret_cast<float*>(base + o);
+  o += 4u * LCAP;
+  f.BX = reinterpret_cast<float*>(base + o);
+  o += 4u * LCAP;
+  f.BI = reinterpret_cast<uint16_t*>(base + o);
+  o += align16(2u * LCAP);
+  f.bm = reinterpret_cast<uint32_t*>(base + o);
   o += align16(4u * (vcap / 32));
-  w.hist = reinterpret_cast<uint32_t*>(base + o);
+  f.wpre = reinterpret_cast<uint16_t*>(base + o);
+  o += align16(2u * (vcap / 32));
+  f.hist = reinterpret_cast<uint32_t*>(base + o);
   o += 4u * 256;
-  w.keys = reinterpret_cast<unsigned long long*>(base + o);
-  return w;
+  f.mbar = reinterpret_cast<uint64_t*>(base + o);
+  f.counter = reinterpret_cast<uint32_t*>(base + o + 8);
+  return f;
 }
 
-// Copies n logits of the row into A as f32 (16-byte vector loads when the row
-// start is aligned).
-template <int DT>
-__device__ void load_row(float* A, const void* base, long long off, int n) {
-  const unsigned lane = lane_id();
-  if (DT == Q3S_DTYPE_F32) {
-    const float* src = static_cast<const float*>(base) + off;
-    int done = 0;
-    if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
-      const int n4 = n >> 2;
-      const float4* s4 = reinterpret_cast<const float4*>(src);
-      float4* a4 = reinterpret_cast<float4*>(A);
-      for (int q = lane; q < n4; q += 32) a4[q] = __ldg(s4 + q);
-      done = n4 << 2;
-    }
-    for (int i = done + lane; i < n; i += 32) A[i] = __ldg(src + i);
+// Per-warp global workspace of the general path.
+struct GenSpace {
+  float* A;      // [vcap] the row, then x
+  float* B;      // [vcap] list values
+  float* BX;     // [vcap] list x
+  uint16_t* BI;  // [vcap] list indices
+};
+
+__host__ __device__ inline size_t gen_bytes(int vcap) {
+  return align16(4u * vcap) * 3 + align16(2u * vcap);
+}
+
+__device__ inline GenSpace carve_gen(unsigned char* base, int vcap) {
+  GenSpace g;
+  g.A = reinterpret_cast<float*>(base);
+  g.B = reinterpret_cast<float*>(base + align16(4u * vcap));
+  g.BX = reinterpret_cast<float*>(base + 2 * align16(4u * vcap));
+  g.BI = reinterpret_cast<uint16_t*>(base + 3 * align16(4u * vcap));
+  return g;
+}
+
+struct RowOut {
+  int status;
+  uint32_t token;
+};
+
+// Where row r's elements sit in the stage: element i at byte mis*es + i*es.
+struct StageView {
+  int n;    // elements
+  int mis;  // leading misalignment in elements
+  int Q;    // 16-byte vectors covering the row
+};
+
+// Row geometry shared by the copy issuer and the consumer.
+struct RowGeom {
+  const unsigned char* p0;  // first byte of the row
+  uint32_t bytes;           // row bytes
+  uint32_t mis_bytes;       // p0 & 15
+  uint32_t head_end;        // bytes [0, head_end) of the row come from plain loads
+  uint32_t tail_begin;      // bytes [tail_begin, bytes) too
+};
+
+__device__ __forceinline__ RowGeom row_geom(const KernelArgs& a, long long row, int n, int es) {
+  RowGeom g;
+  const long long off = a.row_offsets ? a.row_offsets[row] : row * a.row_stride;
+  g.p0 = static_cast<const unsigned char*>(a.logits) + off * es;
+  g.bytes = (uint32_t)n * es;
+  const uintptr_t s = reinterpret_cast<uintptr_t>(g.p0);
+  g.mis_bytes = (uint32_t)(s & 15u);
+  const uintptr_t a0 = (s + 15u) & ~(uintptr_t)15u;
+  const uintptr_t a1 = (s + g.bytes) & ~(uintptr_t)15u;
+  if (a1 > a0) {
+    g.head_end = (uint32_t)(a0 - s);
+    g.tail_begin = (uint32_t)(a1 - s);
   } else {
-    const unsigned short* src = static_cast<const unsigned short*>(base) + off;
-    int done = 0;
-    if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
-      const int n8 = n >> 3;
-      const uint4* s8 = reinterpret_cast<const uint4*>(src);
-      float4* a4 = reinterpret_cast<float4*>(A);
-      for (int q = lane; q < n8; q += 32) {
-        const uint4 v = __ldg(s8 + q);
-        a4[2 * q] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
-                                __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
-        a4[2 * q + 1] =
-            make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u),
-                        __uint_as_float(v.w << 16), __uint_as_float(v.w & 0xFFFF0000u));
-      }
-      done = n8 << 3;
-    }
-    for (int i = done + lane; i < n; i += 32) A[i] = load_elem<Q3S_DTYPE_BF16>(src, i);
+    g.head_end = g.bytes;
+    g.tail_begin = g.bytes;
+  }
+  return g;
+}
+
+__device__ __forceinline__ int row_vocab(const KernelArgs& a, long long row) {
+  return a.row_vocab ? a.row_vocab[row] : a.vocab;
+}
+
+__device__ __forceinline__ bool row_fits(const KernelArgs& a, int n) {
+  return n >= 0 && n <= a.vocab && n <= a.vcap;
+}
+
+// Lane 0: arms the stage barrier and starts the interior bulk copy of `row`.
+// Rows that do not fit the stage arm the barrier with no bytes.
+template <int DT>
+__device__ void issue_row(const KernelArgs& a, long long row, const FastSpace& f) {
+  constexpr int es = Elem<DT>::BYTES;
+  const int n = row_vocab(a, row);
+  uint32_t bytes = 0;
+  RowGeom g;
+  if (row_fits(a, n)) {
+    g = row_geom(a, row, n, es);
+    bytes = g.tail_begin - g.head_end;
+  }
+  mbar_arrive_expect_tx(f.mbar, bytes);
+  if (bytes > 0) bulk_copy_g2s(f.stage + g.mis_bytes + g.head_end, g.p0 + g.head_end, bytes, f.mbar);
+}
+
+// After the barrier completes: the lanes copy the unaligned head and tail.
+template <int DT>
+__device__ StageView complete_stage(const KernelArgs& a, long long row, int n, const FastSpace& f) {
+  constexpr int es = Elem<DT>::BYTES;
+  const RowGeom g = row_geom(a, row, n, es);
+  const unsigned lane = lane_id();
+  const int hn = (int)(g.head_end / es);
+  const int t0 = (int)(g.tail_begin / es);
+  for (int i = lane; i < hn; i += 32) {
+    if (es == 4)
+      reinterpret_cast<float*>(f.stage + g.mis_bytes)[i] = __ldg(reinterpret_cast<const float*>(g.p0) + i);
+    else
+      reinterpret_cast<unsigned short*>(f.stage + g.mis_bytes)[i] =
+          __ldg(reinterpret_cast<const unsigned short*>(g.p0) + i);
+  }
+  for (int i = t0 + lane; i < n; i += 32) {
+    if (es == 4)
+      reinterpret_cast<float*>(f.stage + g.mis_bytes)[i] = __ldg(reinterpret_cast<const float*>(g.p0) + i);
+    else
+      reinterpret_cast<unsigned short*>(f.stage + g.mis_bytes)[i] =
+          __ldg(reinterpret_cast<const unsigned short*>(g.p0) + i);
   }
   __syncwarp();
+  StageView v;
+  v.n = n;
+  v.mis = (int)(g.mis_bytes / es);
+  v.Q = (int)((g.mis_bytes + g.bytes + 15u) / 16u);
+  return v;
+}
+
+template <int DT>
+__device__ __forceinline__ void unpack(const unsigned char* stage, int q, float (&e)[Elem<DT>::EPV]) {
+  const uint4 v = *reinterpret_cast<const uint4*>(stage + 16 * q);
+  if (DT == Q3S_DTYPE_F32) {
+    e[0] = __uint_as_float(v.x);
+    e[1] = __uint_as_float(v.y);
+    e[2] = __uint_as_float(v.z);
+    e[3] = __uint_as_float(v.w);
+  } else {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      e[2 * t] = __uint_as_float(w[t] << 16);
+      e[2 * t + 1] = __uint_as_float(w[t] & 0xFFFF0000u);
+    }
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ float stage_elem(const unsigned char* stage, int mis, int i) {
+  if (DT == Q3S_DTYPE_F32) return reinterpret_cast<const float*>(stage)[mis + i];
+  return __uint_as_float(((uint32_t) reinterpret_cast<const unsigned short*>(stage)[mis + i]) << 16);
 }
 
 // Option validation of sampling.rs:281-296 (f64 comparisons).
@@ -117,16 +264,40 @@ __device__ __forceinline__ bool idx_allowed(int i, int sf, int allow) {
   return sf < 0 || i < sf || (allow >= 0 && i == allow);
 }
 
+// Per-row transform inputs.
+struct RowCtx {
+  int n, mis, Q;
+  float inv;      // 1 / (temperature as f32)
+  float pf;       // repetition penalty as f32
+  bool use_pen;
+  int sf, allow;
+  const uint32_t* bm;
+};
+
+// x of element i from its raw value v.  XF: penalty, mask and temperature of
+// sampling.rs:598-631.  Without XF the raw value is returned (rows with no
+// penalty and no suppression select on raw values and scale afterwards).
+template <bool XF, bool EDGE>
+__device__ __forceinline__ float xform(float v, int i, const RowCtx& r) {
+  if (EDGE && (unsigned)i >= (unsigned)r.n) return neg_inf();
+  if (!XF) return v;
+  if (r.use_pen && ((r.bm[i >> 5] >> (i & 31)) & 1u))
+    v = v < 0.0f ? __fmul_rn(v, r.pf) : __fdiv_rn(v, r.pf);
+  const bool sup = r.sf >= 0 && i >= r.sf && i != r.allow;
+  if (!is_finite(v) || sup) v = neg_inf();
+  return __fmul_rn(v, r.inv);
+}
+
 // k-th smallest (1-based) key among the valid elements, MSB-first radix
-// selection with 8-bit digits.  Requires at least k valid elements.
+// selection with 8-bit digits from bit `top_shift + 8` down.  Requires at
+// least k valid elements whose keys are below 2^(top_shift + 8).
 template <typename K, class KeyFn>
-__device__ K warp_select(int n, uint32_t k, KeyFn keyfn, uint32_t* hist) {
-  constexpr int BITS = 8 * sizeof(K);
+__device__ K warp_select(int n, uint32_t k, KeyFn keyfn, uint32_t* hist, int top_shift) {
   const unsigned lane = lane_id();
   K prefix = 0, mask = 0;
   uint32_t kk = k;
 #pragma unroll 1
-  for (int shift = BITS - 8; shift >= 0; shift -= 8) {
+  for (int shift = top_shift; shift >= 0; shift -= 8) {
     for (int b = lane; b < 256; b += 32) hist[b] = 0u;
     __syncwarp();
     for (int i = lane; i < n; i += 32) {
@@ -144,8 +315,8 @@ __device__ K warp_select(int n, uint32_t k, KeyFn keyfn, uint32_t* hist) {
     }
     const uint32_t incl = warp_inclusive_scan(s);
     const unsigned ball = __ballot_sync(FULL, incl >= kk);
-    const int src = __ffs(ball) - 1;
-    uint32_t digit = 0, before = 0;
+    const int src = ball ? __ffs(ball) - 1 : 31;
+    uint32_t digit = 255, before = 0;
     if ((int)lane == src) {
       uint32_t acc = incl - s;
 #pragma unroll
@@ -224,143 +395,28 @@ __device__ __forceinline__ unsigned long long nucleus_key(float p, uint16_t idx)
   return ((unsigned long long)(~__float_as_uint(p)) << 32) | idx;
 }
 
-struct RowOut {
-  int status;
-  uint32_t token;
+// Debug outputs of one row (probs and masks), NULL when not requested.
+struct DebugRow {
+  unsigned char* masks;
+  float* probs;
 };
 
-template <int DT>
-__device__ RowOut sample_row(const KernelArgs& a, const WarpSpace& w, long long row, int n,
-                             const q3s_row_params& P) {
+// Top-p, final softmax and draw over a survivor list in vocabulary order:
+// B[j] = exp(x_j - m1), BX[j] = x_j, BI[j] = index, m1 = max x (sampling.rs:665-729).
+__device__ RowOut finish_list(float* B, float* BX, uint16_t* BI, int ns, float m1,
+                              const q3s_row_params& P, unsigned long long* keys, uint32_t* hist,
+                              float u, int n, const DebugRow& dbg) {
   const unsigned lane = lane_id();
-  const long long off = a.row_offsets ? a.row_offsets[row] : row * a.row_stride;
-  float* A = w.A;
-  float* B = w.B;
-  uint16_t* BI = w.BI;
-  const int sf = P.suppress_from, allow = P.allow_token;
-  const bool dbg = a.masks != nullptr;
-  unsigned char* mrow = dbg ? a.masks + row * a.probs_stride : nullptr;
-  float* prow = a.probs ? a.probs + row * a.probs_stride : nullptr;
-  if (dbg)
-    for (int i = lane; i < n; i += 32) mrow[i] = 0;
-  if (prow)
-    for (int i = lane; i < n; i += 32) prow[i] = 0.0f;
-
-  load_row<DT>(A, a.logits, off, n);
-
-  // Greedy (sampling.rs:574-591): total_cmp maximum of the raw finite,
-  // allowed logits; ties to the lowest index; no penalty, no draw.
-  if (!P.do_sample) {
-    unsigned long long best = 0ull;
-    for (int i = lane; i < n; i += 32) {
-      const float v = A[i];
-      if (is_finite(v) && idx_allowed(i, sf, allow)) {
-        const unsigned long long c =
-            ((unsigned long long)total_key(v) << 32) | (0xFFFFFFFFu - (uint32_t)i);
-        best = c > best ? c : best;
-      }
-    }
-    best = warp_max_u64(best);
-    if (best == 0ull) return {Q3S_STATUS_NO_CANDIDATE, 0u};
-    return {Q3S_STATUS_OK, 0xFFFFFFFFu - (uint32_t)best};
-  }
-
-  // Repetition penalty (sampling.rs:598-606, 732-773): every distinct history
-  // id < n once, marked in a bitmap.
-  long long h0 = 0, h1 = 0;
-  if (a.history_offsets) {
-    h0 = a.history_offsets[row];
-    h1 = a.history_offsets[row + 1];
-  }
-  const bool use_pen = P.repetition_penalty != 1.0 && h1 > h0;
-  const float pf = (float)P.repetition_penalty;
-  if (use_pen) {
-    const int words = (n + 31) >> 5;
-    for (int q = lane; q < words; q += 32) w.bm[q] = 0u;
-    __syncwarp();
-    for (long long h = h0 + lane; h < h1; h += 32) {
-      const int id = a.history[h];
-      if (id < n) atomicOr(&w.bm[id >> 5], 1u << (id & 31));
-    }
-    __syncwarp();
-  }
-
-  // Mask and temperature (sampling.rs:608-631).
-  const float inv_temp = __fdiv_rn(1.0f, (float)P.temperature);
-  float mx = neg_inf();
-  int nfin = 0;
-  bool nan_seen = false;
-  for (int i = lane; i < n; i += 32) {
-    float v = A[i];
-    if (use_pen && ((w.bm[i >> 5] >> (i & 31)) & 1u))
-      v = v < 0.0f ? __fmul_rn(v, pf) : __fdiv_rn(v, pf);
-    const bool suppressed = sf >= 0 && i >= sf && !(allow >= 0 && i == allow);
-    if (!is_finite(v) || suppressed) v = neg_inf();
-    const float x = __fmul_rn(v, inv_temp);
-    A[i] = x;
-    mx = fmaxf(mx, x);
-    nfin += is_finite(x) ? 1 : 0;
-    nan_seen |= (x != x);
-    if (dbg && is_finite(x)) mrow[i] = 1;
-  }
-  mx = warp_max(mx);
-  nfin = __reduce_add_sync(FULL, nfin);
-  nan_seen = __any_sync(FULL, nan_seen);
-  __syncwarp();
-  // No finite candidate (sampling.rs:642-651).
-  if (nfin == 0)
-    return {sf >= 0 ? Q3S_STATUS_SUPPRESSION_NO_CANDIDATE : Q3S_STATUS_NO_CANDIDATE, 0u};
-  // A NaN or +inf after the temperature survives top-k and top-p and makes
-  // the softmax denominator non-finite (sampling.rs:675-678, 715-718).
-  if (nan_seen || mx == __int_as_float(0x7f800000)) return {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
-
-  // Top-k threshold: the k-th largest finite value (sampling.rs:654-663).
-  float t = neg_inf();
-  if (P.top_k > 0u && (uint32_t)nfin > P.top_k) {
-    const uint32_t key = warp_select<uint32_t>(
-        n, P.top_k,
-        [&](int i, uint32_t& k) {
-          const float x = A[i];
-          k = ~total_key(x);
-          return x > neg_inf();
-        },
-        w.hist);
-    t = from_total_key(~key);
-  }
-  auto survives = [&](float x) { return x >= t && x > neg_inf(); };
-  if (dbg) {
-    for (int i = lane; i < n; i += 32)
-      if (survives(A[i])) mrow[i] |= 2;
-  }
-
-  // Candidate list in vocabulary order.  With top-p the values are
-  // exp(x - max) of the denominator; otherwise those of the final softmax.
-  const float m1 = mx;
-  int ns = 0;
-  for (int i0 = 0; i0 < n; i0 += 32) {
-    const int i = i0 + lane;
-    const bool p = i < n && survives(A[i]);
-    const unsigned b = __ballot_sync(FULL, p);
-    if (p) {
-      const int j = ns + __popc(b & lanemask_lt());
-      BI[j] = (uint16_t)i;
-      B[j] = cr_expf(__fsub_rn(A[i], m1));
-    }
-    ns += __popc(b);
-  }
-  __syncwarp();
-
   float m2 = m1;
   if (P.top_p < 1.0) {
-    // Top-p (sampling.rs:665-698).  Denominator: sequential f32 sum in
-    // vocabulary order; max_logit is m1 because the maximum survives top-k.
+    // Denominator: sequential f32 sum in vocabulary order.
     const float total = chain_sum(B, ns, false);
     if (!is_finite(total) || total <= 0.0f) return {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
     const float inv_total = __fdiv_rn(1.0f, total);
     const float cutoff = __fsub_rn(m1, 16.0f);
     int np = 0;
     for (int j = lane; j < ns; j += 32) {
-      const float p = A[BI[j]] >= cutoff ? __fmul_rn(B[j], inv_total) : 0.0f;
+      const float p = BX[j] >= cutoff ? __fmul_rn(B[j], inv_total) : 0.0f;
       B[j] = p;
       np += p > 0.0f ? 1 : 0;
     }
@@ -383,31 +439,35 @@ __device__ RowOut sample_row(const KernelArgs& a, const WarpSpace& w, long long 
     while (remaining > 0) {
       const int m = remaining < 256 ? remaining : 256;
       unsigned long long hi = ~0ull;
-      if (remaining > 256) hi = warp_select<unsigned long long>(ns, 256u, pkey, w.hist);
+      if (remaining > 256) hi = warp_select<unsigned long long>(ns, 256u, pkey, hist, 56);
       int cnt = 0;
       for (int j0 = 0; j0 < ns; j0 += 32) {
         const int j = j0 + lane;
         unsigned long long k = 0;
         const bool p = j < ns && pkey(j, k) && k <= hi;
         const unsigned b = __ballot_sync(FULL, p);
-        if (p) w.keys[cnt + __popc(b & lanemask_lt())] = k;
+        if (p) {
+          const int d = cnt + __popc(b & lanemask_lt());
+          if (d < 256) keys[d] = k;
+        }
         cnt += __popc(b);
       }
+      if (cnt > 256) cnt = 256;
       __syncwarp();
       unsigned long long v[8];
 #pragma unroll
       for (int r = 0; r < 8; ++r) {
         const int e = lane * 8 + r;
-        v[r] = e < cnt ? w.keys[e] : ~0ull;
+        v[r] = e < cnt ? keys[e] : ~0ull;
       }
       __syncwarp();
       bitonic_sort_256(v);
 #pragma unroll
-      for (int r = 0; r < 8; ++r) w.keys[lane * 8 + r] = v[r];
+      for (int r = 0; r < 8; ++r) keys[lane * 8 + r] = v[r];
       __syncwarp();
       if (lane == 0) {
         for (int q = 0; q < cnt; ++q) {
-          const unsigned long long k = w.keys[q];
+          const unsigned long long k = keys[q];
           const float p = __uint_as_float(~(uint32_t)(k >> 32));
           if (pos > 0 && cum >= top_p) {
             cut = k;
@@ -420,6 +480,7 @@ __device__ RowOut sample_row(const KernelArgs& a, const WarpSpace& w, long long 
       cut = __shfl_sync(FULL, cut, 0);
       cum = __shfl_sync(FULL, cum, 0);
       pos = __shfl_sync(FULL, pos, 0);
+      __syncwarp();
       if (cut != ~0ull) break;
       last = hi;
       remaining -= m;
@@ -429,7 +490,7 @@ __device__ RowOut sample_row(const KernelArgs& a, const WarpSpace& w, long long 
     for (int j = lane; j < ns; j += 32) {
       const float p = B[j];
       if (p > 0.0f && nucleus_key(p, BI[j]) >= cut) B[j] = 0.0f;
-      if (B[j] > 0.0f) m2 = fmaxf(m2, A[BI[j]]);
+      if (B[j] > 0.0f) m2 = fmaxf(m2, BX[j]);
     }
     m2 = warp_max(m2);
     __syncwarp();
@@ -440,12 +501,14 @@ __device__ RowOut sample_row(const KernelArgs& a, const WarpSpace& w, long long 
       const int j = j0 + lane;
       const bool p = j < ns && B[j] > 0.0f;
       const int i = p ? BI[j] : 0;
+      const float x = p ? BX[j] : 0.0f;
       __syncwarp();
       const unsigned b = __ballot_sync(FULL, p);
       if (p) {
         const int d = ns2 + __popc(b & lanemask_lt());
         BI[d] = (uint16_t)i;
-        B[d] = cr_expf(__fsub_rn(A[i], m2));
+        BX[d] = x;
+        B[d] = cr_expf(__fsub_rn(x, m2));
       }
       ns2 += __popc(b);
       __syncwarp();
@@ -456,8 +519,6 @@ __device__ RowOut sample_row(const KernelArgs& a, const WarpSpace& w, long long 
   // Final softmax sum and the draw (sampling.rs:700-729).
   const float sum = chain_sum(B, ns, true);
   if (!is_finite(sum) || sum <= 0.0f) return {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
-  const float u = a.uniform_override ? a.uniform_override[row]
-                                     : philox_uniform(a.seeds[row], a.subseqs[row], P.ctr_lo);
   const float thr = __fmul_rn(u, sum);
   int first = ns;
   for (int j = lane; j < ns; j += 32) {
@@ -469,35 +530,477 @@ __device__ RowOut sample_row(const KernelArgs& a, const WarpSpace& w, long long 
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) first = min(first, __shfl_xor_sync(FULL, first, o));
   const uint32_t token = first < ns ? (uint32_t)BI[first] : (uint32_t)(n - 1);
-  if (dbg || prow) {
+  if (dbg.masks || dbg.probs) {
     for (int j = lane; j < ns; j += 32) {
       const int i = BI[j];
-      if (dbg) mrow[i] |= 4;
-      if (prow) {
-        const float e = cr_expf(__fsub_rn(A[i], m2));
-        prow[i] = __double2float_rn((double)e / (double)sum);
+      if (dbg.masks) dbg.masks[i] |= 4;
+      if (dbg.probs) {
+        const float e = cr_expf(__fsub_rn(BX[j], m2));
+        dbg.probs[i] = __double2float_rn((double)e / (double)sum);
       }
     }
   }
+  __syncwarp();
   return {Q3S_STATUS_OK, token};
 }
 
+// ---------------------------------------------------------------------------
+// Row handlers.  Each releases the stage (`release`) exactly once, as soon as
+// it no longer reads it.
+// ---------------------------------------------------------------------------
+struct Releaser {
+  const KernelArgs* a;
+  const FastSpace* f;
+  long long next;
+  bool done;
+};
+
 template <int DT>
+__device__ __forceinline__ void release(Releaser& r) {
+  if (r.done) return;
+  r.done = true;
+  __syncwarp();
+  if (lane_id() == 0) {
+    fence_proxy_async_smem();
+    if (r.next < r.a->num_rows) issue_row<DT>(*r.a, r.next, *r.f);
+  }
+}
+
+// Greedy row (sampling.rs:574-591) straight from the stage.
+template <int DT>
+__device__ RowOut greedy_stage(const FastSpace& f, const StageView& s, int sf, int allow) {
+  constexpr int EPV = Elem<DT>::EPV;
+  const unsigned lane = lane_id();
+  unsigned long long best = 0ull;
+  for (int q = lane; q < s.Q; q += 32) {
+    float e[EPV];
+    unpack<DT>(f.stage, q, e);
+#pragma unroll
+    for (int c = 0; c < EPV; ++c) {
+      const int i = q * EPV + c - s.mis;
+      if ((unsigned)i < (unsigned)s.n && is_finite(e[c]) && idx_allowed(i, sf, allow)) {
+        const unsigned long long k =
+            ((unsigned long long)total_key(e[c]) << 32) | (0xFFFFFFFFu - (uint32_t)i);
+        best = k > best ? k : best;
+      }
+    }
+  }
+  best = warp_max_u64(best);
+  if (best == 0ull) return {Q3S_STATUS_NO_CANDIDATE, 0u};
+  return {Q3S_STATUS_OK, 0xFFFFFFFFu - (uint32_t)best};
+}
+
+// General path: the full row as f32 in the global workspace, then full-row
+// passes (any top_k, any temperature).
+template <int DT>
+__device__ RowOut general_row(const FastSpace& f, const GenSpace& g, const StageView& s,
+                              const q3s_row_params& P, const RowCtx& rc, float u, Releaser& rel,
+                              const DebugRow& dbg) {
+  const unsigned lane = lane_id();
+  const int n = s.n;
+  float* A = g.A;
+  for (int i = lane; i < n; i += 32) A[i] = stage_elem<DT>(f.stage, s.mis, i);
+  __syncwarp();
+  release<DT>(rel);
+  // Mask and temperature (sampling.rs:608-631).
+  float mx = neg_inf();
+  int nfin = 0;
+  bool nan_seen = false;
+  for (int i = lane; i < n; i += 32) {
+    const float x = xform<true, false>(A[i], i, rc);
+    A[i] = x;
+    mx = fmaxf(mx, x);
+    nfin += is_finite(x) ? 1 : 0;
+    nan_seen |= (x != x);
+    if (dbg.masks && is_finite(x)) dbg.masks[i] = 1;
+  }
+  mx = warp_max(mx);
+  nfin = __reduce_add_sync(FULL, nfin);
+  nan_seen = __any_sync(FULL, nan_seen);
+  __syncwarp();
+  if (nfin == 0)
+    return {rc.sf >= 0 ? Q3S_STATUS_SUPPRESSION_NO_CANDIDATE : Q3S_STATUS_NO_CANDIDATE, 0u};
+  // A NaN or +inf after the temperature survives top-k and top-p and makes
+  // the softmax denominator non-finite (sampling.rs:675-678, 715-718).
+  if (nan_seen || mx == __int_as_float(0x7f800000)) return {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
+  // Top-k threshold: the k-th largest finite value (sampling.rs:654-663).
+  float t = neg_inf();
+  if (P.top_k > 0u && (uint32_t)nfin > P.top_k) {
+    const uint32_t key = warp_select<uint32_t>(
+        n, P.top_k,
+        [&](int i, uint32_t& k) {
+          const float x = A[i];
+          k = ~total_key(x);
+          return x > neg_inf();
+        },
+        f.hist, 24);
+    t = from_total_key(~key);
+  }
+  // Survivor list in vocabulary order.
+  int ns = 0;
+  for (int i0 = 0; i0 < n; i0 += 32) {
+    const int i = i0 + lane;
+    const float x = i < n ? A[i] : neg_inf();
+    const bool p = x >= t && x > neg_inf();
+    const unsigned b = __ballot_sync(FULL, p);
+    if (p) {
+      const int j = ns + __popc(b & lanemask_lt());
+      g.BI[j] = (uint16_t)i;
+      g.BX[j] = x;
+      g.B[j] = cr_expf(__fsub_rn(x, mx));
+      if (dbg.masks) dbg.masks[i] |= 2;
+    }
+    ns += __popc(b);
+  }
+  __syncwarp();
+  return finish_list(g.B, g.BX, g.BI, ns, mx, P, reinterpret_cast<unsigned long long*>(f.cand),
+                     f.hist, u, n, dbg);
+}
+
+// Vector maxima of the stage (registers) and the row maximum.
+template <int DT, int NJ, bool XF, bool EDGE>
+__device__ __forceinline__ float scan_stage(const FastSpace& f, const RowCtx& r, float (&vm)[NJ]) {
+  constexpr int EPV = Elem<DT>::EPV;
+  const int lane = (int)lane_id();
+  float mx = neg_inf();
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const int q = lane + 32 * j;
+    float m = neg_inf();
+    if (q < r.Q) {
+      float e[EPV];
+      unpack<DT>(f.stage, q, e);
+#pragma unroll
+      for (int c = 0; c < EPV; ++c) m = fmaxf(m, xform<XF, EDGE>(e[c], q * EPV + c - r.mis, r));
+    }
+    vm[j] = m;
+    mx = fmaxf(mx, m);
+  }
+  return warp_max(mx);
+}
+
+template <int NJ>
+__device__ __forceinline__ int count_ge(const float (&vm)[NJ], float tau) {
+  int c = 0;
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) c += vm[j] >= tau ? 1 : 0;
+  return (int)__reduce_add_sync(FULL, (unsigned)c);
+}
+
+// Candidates {x >= tau} of the flagged vectors into f.cand (x after the
+// temperature, index); returns their count (may exceed CAP: overflow).
+template <int DT, int NJ, bool XF, bool EDGE>
+__device__ int collect(const FastSpace& f, const RowCtx& r, const float (&vm)[NJ], float tau) {
+  constexpr int EPV = Elem<DT>::EPV;
+  const int lane = (int)lane_id();
+  if (lane == 0) *f.counter = 0u;
+  __syncwarp();
+  uint64_t flags = 0;
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) flags |= (vm[j] >= tau ? 1ull : 0ull) << j;
+  while (flags) {
+    const int j = __ffsll((long long)flags) - 1;
+    flags &= flags - 1;
+    const int q = lane + 32 * j;
+    float e[EPV];
+    unpack<DT>(f.stage, q, e);
+    float x[EPV];
+    int cnt = 0;
+#pragma unroll
+    for (int c = 0; c < EPV; ++c) {
+      x[c] = xform<XF, EDGE>(e[c], q * EPV + c - r.mis, r);
+      cnt += x[c] >= tau ? 1 : 0;
+    }
+    uint32_t pos = atomicAdd(f.counter, (uint32_t)cnt);
+#pragma unroll
+    for (int c = 0; c < EPV; ++c) {
+      if (x[c] >= tau) {
+        if (pos < (uint32_t)CAP) {
+          const float xv = XF ? x[c] : __fmul_rn(x[c], r.inv);
+          f.cand[pos] = make_uint2(__float_as_uint(xv), (uint32_t)(q * EPV + c - r.mis));
+        }
+        ++pos;
+      }
+    }
+  }
+  __syncwarp();
+  const int c = (int)*f.counter;
+  __syncwarp();
+  return c;
+}
+
+// Debug pass over the stage: bit0 finite x, bit1 x >= t.
+template <int DT, bool XF>
+__device__ void debug_masks(const FastSpace& f, const RowCtx& r, float t, unsigned char* masks) {
+  const unsigned lane = lane_id();
+  for (int i = lane; i < r.n; i += 32) {
+    float x = xform<XF, false>(stage_elem<DT>(f.stage, r.mis, i), i, r);
+    if (!XF) x = is_finite(x) ? __fmul_rn(x, r.inv) : neg_inf();
+    unsigned char m = 0;
+    if (is_finite(x)) m = 1;
+    if (is_finite(x) && x >= t) m |= 2;
+    masks[i] = m;
+  }
+  __syncwarp();
+}
+
+// Fast path; returns false (before releasing the stage) when the row must
+// take the general path instead.
+template <int DT, int NJ, bool XF, bool EDGE>
+__device__ bool fast_row(const FastSpace& f, const StageView& s, const q3s_row_params& P,
+                         const RowCtx& rc, float u, Releaser& rel, const DebugRow& dbg,
+                         float& delta, RowOut& out) {
+  const unsigned lane = lane_id();
+  const int n = s.n;
+  float vm[NJ];
+  const float mx = scan_stage<DT, NJ, XF, EDGE>(f, rc, vm);
+  // Row maximum in the x domain.
+  if (!XF && mx == __int_as_float(0x7f800000)) return false;  // raw +inf: general path
+  if (mx == neg_inf() || mx != mx) {
+    release<DT>(rel);
+    out = {rc.sf >= 0 ? Q3S_STATUS_SUPPRESSION_NO_CANDIDATE : Q3S_STATUS_NO_CANDIDATE, 0u};
+    return true;
+  }
+  const float Mx = XF ? mx : __fmul_rn(mx, rc.inv);
+  if (Mx == __int_as_float(0x7f800000)) {
+    release<DT>(rel);
+    out = {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
+    return true;
+  }
+  // Threshold on the vector maxima: count in [k, hi].
+  const int k = (int)P.top_k;
+  const int hi = k <= 128 ? max(2 * k, 64) : k + 96;
+  float vmin = __int_as_float(0x7f800000);
+#pragma unroll
+  for (int j = 0; j < NJ; ++j)
+    if (vm[j] > neg_inf()) vmin = fminf(vmin, vm[j]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) vmin = fminf(vmin, __shfl_xor_sync(FULL, vmin, o));
+  const float span = __fsub_rn(mx, vmin);
+  if (!(span < __int_as_float(0x7f800000))) return false;
+  if (count_ge(vm, vmin) < k) return false;  // fewer than k finite vectors
+  float lo = 0.0f, hiD = span;
+  bool hi_known = false;
+  float d = (delta > 0.0f && delta <= span) ? delta : span * 0.25f;
+  float best = span;  // smallest distance seen whose count reaches k
+  bool accepted = false;
+#pragma unroll 1
+  for (int it = 0; it < 24; ++it) {
+    const int c = count_ge(vm, __fsub_rn(mx, d));
+    if (c >= k) best = fminf(best, d);
+    if (c < k) {
+      lo = d;
+      d = hi_known ? 0.5f * (lo + hiD) : fminf(span, d > 0.0f ? 2.0f * d : span * 0.0625f);
+    } else if (c > hi) {
+      hiD = d;
+      hi_known = true;
+      d = 0.5f * (lo + hiD);
+    } else {
+      accepted = true;
+      break;
+    }
+    if (hiD - lo <= 0.0f) break;
+  }
+  if (!accepted) d = best;
+  float tau = __fsub_rn(mx, d);
+  // Raw-domain selection: lower tau until its image lies strictly below the
+  // image of every value that reaches the chosen count, so no element with
+  // v < tau can tie the k-th largest x after the multiply.
+  if (!XF && rc.inv != 1.0f) {
+    const float img = __fmul_rn(tau, rc.inv);
+    float t2 = tau;
+    bool ok = false;
+#pragma unroll 1
+    for (int it = 0; it < 8 && !ok; ++it) {
+      t2 = __fsub_rn(t2, fmaxf(fabsf(t2) * 3.814697265625e-06f, 1.1754944e-38f));
+      ok = __fmul_rn(t2, rc.inv) < img;
+    }
+    if (!ok) return false;
+    tau = t2;
+  }
+  const int c = collect<DT, NJ, XF, EDGE>(f, rc, vm, tau);
+  if (c > CAP || c < k) return false;
+  delta = d;
+  if (!dbg.masks) release<DT>(rel);
+
+  // Exact k-th largest candidate: keys relative to the largest key.
+  uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+  for (int j = lane; j < c; j += 32) {
+    const uint32_t kk = total_key(__uint_as_float(f.cand[j].x));
+    kmin = min(kmin, kk);
+    kmax = max(kmax, kk);
+  }
+  kmin = __reduce_min_sync(FULL, kmin);
+  kmax = __reduce_max_sync(FULL, kmax);
+  const uint32_t kspan = kmax - kmin;
+  float t;
+  if (kspan == 0u) {
+    t = from_total_key(kmax);
+  } else {
+    const int bits = 32 - __clz(kspan);
+    const int top = ((bits + 7) / 8) * 8 - 8;
+    const uint32_t rel_k = warp_select<uint32_t>(
+        c, (uint32_t)k,
+        [&](int j, uint32_t& key) {
+          key = kmax - total_key(__uint_as_float(f.cand[j].x));
+          return true;
+        },
+        f.hist, top);
+    t = from_total_key(kmax - rel_k);
+  }
+  // Survivors x >= t, in vocabulary order through a bitmap.
+  const int words = (n + 31) >> 5;
+  for (int w = lane; w < words; w += 32) f.bm[w] = 0u;
+  __syncwarp();
+  for (int j = lane; j < c; j += 32) {
+    const uint2 e = f.cand[j];
+    if (__uint_as_float(e.x) >= t) atomicOr(&f.bm[e.y >> 5], 1u << (e.y & 31));
+  }
+  __syncwarp();
+  const int per = (words + 31) >> 5;
+  const int w0 = min(words, (int)lane * per), w1 = min(words, w0 + per);
+  int mine = 0;
+  for (int w = w0; w < w1; ++w) mine += __popc(f.bm[w]);
+  const int incl = (int)warp_inclusive_scan((uint32_t)mine);
+  int run = incl - mine;
+  for (int w = w0; w < w1; ++w) {
+    f.wpre[w] = (uint16_t)run;
+    run += __popc(f.bm[w]);
+  }
+  const int ns = __shfl_sync(FULL, incl, 31);
+  __syncwarp();
+  for (int j = lane; j < c; j += 32) {
+    const uint2 e = f.cand[j];
+    const float x = __uint_as_float(e.x);
+    if (x >= t) {
+      const uint32_t w = e.y >> 5, b = e.y & 31;
+      const int p = f.wpre[w] + __popc(f.bm[w] & ((1u << b) - 1u));
+      f.BI[p] = (uint16_t)e.y;
+      f.BX[p] = x;
+      f.B[p] = cr_expf(__fsub_rn(x, Mx));
+    }
+  }
+  __syncwarp();
+  if (dbg.masks) debug_masks<DT, XF>(f, rc, t, dbg.masks);
+  out = finish_list(f.B, f.BX, f.BI, ns, Mx, P, reinterpret_cast<unsigned long long*>(f.cand),
+                    f.hist, u, n, dbg);
+  release<DT>(rel);
+  return true;
+}
+
+template <int DT, int NJ>
+__device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const GenSpace& g,
+                              long long row, const StageView& s, const q3s_row_params& P,
+                              Releaser& rel, float& delta, const DebugRow& dbg) {
+  RowCtx rc;
+  rc.n = s.n;
+  rc.mis = s.mis;
+  rc.Q = s.Q;
+  rc.inv = __fdiv_rn(1.0f, (float)P.temperature);
+  rc.pf = (float)P.repetition_penalty;
+  rc.sf = P.suppress_from;
+  rc.allow = P.allow_token;
+  rc.bm = f.bm;
+  long long h0 = 0, h1 = 0;
+  if (a.history_offsets) {
+    h0 = a.history_offsets[row];
+    h1 = a.history_offsets[row + 1];
+  }
+  rc.use_pen = P.repetition_penalty != 1.0 && h1 > h0;
+  const float u = a.uniform_override ? a.uniform_override[row]
+                                     : philox_uniform(a.seeds[row], a.subseqs[row], P.ctr_lo);
+  const bool inv_ok = rc.inv > 0.0f && rc.inv < __int_as_float(0x7f800000);
+  const bool fast = inv_ok && P.top_k >= 1u && P.top_k <= (uint32_t)FAST_MAX_K &&
+                    P.top_k < (uint32_t)s.n;
+  if (fast) {
+    const bool xf = rc.use_pen || rc.sf >= 0;
+    const bool edge = s.mis != 0 || (s.n % Elem<DT>::EPV) != 0;
+    RowOut out;
+    bool done;
+    if (xf)
+      done = edge ? fast_row<DT, NJ, true, true>(f, s, P, rc, u, rel, dbg, delta, out)
+                  : fast_row<DT, NJ, true, false>(f, s, P, rc, u, rel, dbg, delta, out);
+    else
+      done = edge ? fast_row<DT, NJ, false, true>(f, s, P, rc, u, rel, dbg, delta, out)
+                  : fast_row<DT, NJ, false, false>(f, s, P, rc, u, rel, dbg, delta, out);
+    if (done) return out;
+  }
+  return general_row<DT>(f, g, s, P, rc, u, rel, dbg);
+}
+
+template <int DT, int NJ>
 __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int es = Elem<DT>::BYTES;
   const int warp = threadIdx.x >> 5;
   const int warps = blockDim.x >> 5;
-  const WarpSpace w = carve(smem + (size_t)warp * warp_space_bytes(a.vcap), a.vcap);
+  const unsigned lane = lane_id();
+  const FastSpace f = carve_fast(smem + (size_t)warp * fast_bytes(a.vcap, es), a.vcap, es);
+  const long long gw = (long long)blockIdx.x * warps + warp;
+  const GenSpace g = carve_gen(a.scratch + (size_t)gw * gen_bytes(a.vcap), a.vcap);
+  if (lane == 0) {
+    mbar_init(f.mbar, 1);
+    fence_mbarrier_init();
+    fence_proxy_async_smem();
+  }
+  __syncwarp();
   const long long stride = (long long)gridDim.x * warps;
-  for (long long row = (long long)blockIdx.x * warps + warp; row < a.num_rows; row += stride) {
-    const int n = a.row_vocab ? a.row_vocab[row] : a.vocab;
+  long long row = gw;
+  if (row < a.num_rows && lane == 0) issue_row<DT>(a, row, f);
+  uint32_t phase = 0;
+  float delta = 0.0f;
+  for (; row < a.num_rows; row += stride) {
+    Releaser rel{&a, &f, row + stride, false};
+    const int n = row_vocab(a, row);
     const q3s_row_params P = a.params[row * a.params_stride];
-    RowOut out{Q3S_STATUS_UNSUPPORTED, 0u};
-    if (n >= 0 && n <= a.vocab && n <= a.vcap) {
-      out.status = validate(P);
-      if (out.status == Q3S_STATUS_OK) out = sample_row<DT>(a, w, row, n, P);
+    int st = row_fits(a, n) ? validate(P) : Q3S_STATUS_UNSUPPORTED;
+    DebugRow dbg{nullptr, nullptr};
+    if (a.masks && st == Q3S_STATUS_OK) dbg.masks = a.masks + row * a.probs_stride;
+    if (a.probs && st == Q3S_STATUS_OK) dbg.probs = a.probs + row * a.probs_stride;
+    if (dbg.masks)
+      for (int i = lane; i < n; i += 32) dbg.masks[i] = 0;
+    if (dbg.probs)
+      for (int i = lane; i < n; i += 32) dbg.probs[i] = 0.0f;
+    // History bitmap of a sampled row with a penalty (filled while the
+    // stage copy is in flight).
+    if (st == Q3S_STATUS_OK && P.do_sample && P.repetition_penalty != 1.0 && a.history_offsets) {
+      const long long h0 = a.history_offsets[row], h1 = a.history_offsets[row + 1];
+      if (h1 > h0) {
+        const int words = (n + 31) >> 5;
+        for (int w = lane; w < words; w += 32) f.bm[w] = 0u;
+        __syncwarp();
+        for (long long h = h0 + lane; h < h1; h += 32) {
+          const int id = a.history[h];
+          if (id < n) atomicOr(&f.bm[id >> 5], 1u << (id & 31));
+        }
+        __syncwarp();
+      }
     }
-    if (lane_id() == 0) {
+    const bool ready = mbar_wait_bounded(f.mbar, phase, WAIT_LIMIT_NS);
+    phase ^= 1u;
+    if (!ready) {
+      // The stage never arrived: mark this warp's remaining rows and stop
+      // after giving the copy in flight another bounded wait.
+      mbar_wait_bounded(f.mbar, phase ^ 1u, WAIT_LIMIT_NS);
+      for (long long r = row; r < a.num_rows; r += stride)
+        if (lane == 0) {
+          a.tokens[r] = 0u;
+          a.status[r] = (unsigned char)Q3S_STATUS_NOT_RUN;
+        }
+      return;
+    }
+    RowOut out{st, 0u};
+    if (st == Q3S_STATUS_OK) {
+      const StageView s = complete_stage<DT>(a, row, n, f);
+      if (!P.do_sample) {
+        out = greedy_stage<DT>(f, s, P.suppress_from, P.allow_token);
+        release<DT>(rel);
+      } else {
+        out = sampled_row<DT, NJ>(a, f, g, row, s, P, rel, delta, dbg);
+      }
+    }
+    release<DT>(rel);
+    if (lane == 0) {
       a.tokens[row] = out.token;
       a.status[row] = (unsigned char)out.status;
     }
@@ -550,31 +1053,43 @@ __global__ void greedy_kernel(const void* logits, long long num_rows, long long 
   }
 }
 
+template <int DT, int NJ>
+cudaError_t launch_t(const KernelArgs& a, int grid, int warps, cudaStream_t stream) {
+  const size_t smem = fast_bytes(a.vcap, Elem<DT>::BYTES) * (size_t)warps;
+  cudaError_t e = cudaFuncSetAttribute(sample_kernel<DT, NJ>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  sample_kernel<DT, NJ><<<grid, warps * 32, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
-size_t sample_smem_per_warp(int vcap) { return warp_space_bytes(vcap); }
+size_t sample_smem_per_warp(int vcap, int dtype) {
+  return fast_bytes(vcap, dtype == Q3S_DTYPE_F32 ? 4 : 2);
+}
 
-int sample_max_warps(int vcap, size_t smem_limit) {
-  const size_t per = warp_space_bytes(vcap);
+size_t sample_scratch_per_warp(int vcap) { return gen_bytes(vcap); }
+
+int sample_max_warps(int vcap, int dtype, size_t smem_limit) {
+  const size_t per = sample_smem_per_warp(vcap, dtype);
   int w = (int)(smem_limit / per);
   return w > MAX_WARPS ? MAX_WARPS : w;
 }
 
 cudaError_t launch_sample(const KernelArgs& a, int grid, int warps, cudaStream_t stream) {
-  const size_t smem = warp_space_bytes(a.vcap) * (size_t)warps;
-  cudaError_t e;
+  // NJ: 16-byte vectors per lane for the largest row (plus one for a
+  // misaligned start).
   if (a.dtype == Q3S_DTYPE_F32) {
-    e = cudaFuncSetAttribute(sample_kernel<Q3S_DTYPE_F32>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    sample_kernel<Q3S_DTYPE_F32><<<grid, warps * 32, smem, stream>>>(a);
-  } else {
-    e = cudaFuncSetAttribute(sample_kernel<Q3S_DTYPE_BF16>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    sample_kernel<Q3S_DTYPE_BF16><<<grid, warps * 32, smem, stream>>>(a);
+    const int q = (a.vcap * 4 + 15) / 16 + 1;
+    if (q <= 32 * 8) return launch_t<Q3S_DTYPE_F32, 8>(a, grid, warps, stream);
+    if (q <= 32 * 17) return launch_t<Q3S_DTYPE_F32, 17>(a, grid, warps, stream);
+    if (q <= 32 * 25) return launch_t<Q3S_DTYPE_F32, 25>(a, grid, warps, stream);
+    return launch_t<Q3S_DTYPE_F32, 33>(a, grid, warps, stream);
   }
-  return cudaGetLastError();
+  const int q = (a.vcap * 2 + 15) / 16 + 1;
+  if (q <= 32 * 9) return launch_t<Q3S_DTYPE_BF16, 9>(a, grid, warps, stream);
+  return launch_t<Q3S_DTYPE_BF16, 17>(a, grid, warps, stream);
 }
 
 cudaError_t launch_greedy(const void* logits, int dtype, long long num_rows, long long row_stride,
