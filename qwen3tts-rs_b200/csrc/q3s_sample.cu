@@ -45,9 +45,10 @@
 namespace q3s {
 namespace {
 
-constexpr int MAX_WARPS = 12;
-constexpr int CAP = 512;   // fast-path candidate capacity per warp
-constexpr int LCAP = 512;  // fast-path survivor-list capacity per warp
+constexpr int MAX_WARPS = 10;
+constexpr int SEG = 24;         // candidate slots per lane (interleaved: slot t of lane l at t*32+l)
+constexpr int CAP = 32 * SEG;   // fast-path candidate capacity per warp
+constexpr int LCAP = 512;       // fast-path survivor-list capacity per warp
 constexpr int FAST_MAX_K = 256;
 constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;  // bounded wait for a stage: 1 s
 
@@ -250,6 +251,30 @@ __device__ __forceinline__ float stage_elem(const unsigned char* stage, int mis,
   return __uint_as_float(((uint32_t) reinterpret_cast<const unsigned short*>(stage)[mis + i]) << 16);
 }
 
+// Everything the kernel reads about a row besides its logits.
+struct RowMeta {
+  q3s_row_params P;
+  int n;
+  long long h0, h1;  // history range
+  unsigned long long seed, subseq;
+  float uo;  // uniform override
+};
+
+__device__ __forceinline__ RowMeta load_meta(const KernelArgs& a, long long row) {
+  RowMeta m;
+  m.n = row_vocab(a, row);
+  m.P = a.params[row * a.params_stride];
+  m.h0 = m.h1 = 0;
+  if (a.history_offsets) {
+    m.h0 = a.history_offsets[row];
+    m.h1 = a.history_offsets[row + 1];
+  }
+  m.seed = a.seeds ? a.seeds[row] : 0ull;
+  m.subseq = a.subseqs ? a.subseqs[row] : 0ull;
+  m.uo = a.uniform_override ? a.uniform_override[row] : 0.0f;
+  return m;
+}
+
 // Option validation of sampling.rs:281-296 (f64 comparisons).
 __device__ inline int validate(const q3s_row_params& p) {
   if (!isfinite(p.repetition_penalty) || p.repetition_penalty <= 0.0)
@@ -375,16 +400,38 @@ __device__ inline void bitonic_sort_256(unsigned long long (&v)[8]) {
 
 // Sequential f32 sum of B[0..count) by lane 0, in order; when `prefix` is set
 // B[j] is replaced by the running sum.  Result broadcast to every lane.
+// B is 16-byte aligned; four terms are loaded at a time, added in order.
 __device__ inline float chain_sum(float* B, int count, bool prefix) {
   float c = 0.0f;
   if (lane_id() == 0) {
+    float4* B4 = reinterpret_cast<float4*>(B);
+    const int n4 = count >> 2;
     if (prefix) {
-      for (int j = 0; j < count; ++j) {
+      for (int q = 0; q < n4; ++q) {
+        float4 v = B4[q];
+        c = __fadd_rn(c, v.x);
+        v.x = c;
+        c = __fadd_rn(c, v.y);
+        v.y = c;
+        c = __fadd_rn(c, v.z);
+        v.z = c;
+        c = __fadd_rn(c, v.w);
+        v.w = c;
+        B4[q] = v;
+      }
+      for (int j = n4 << 2; j < count; ++j) {
         c = __fadd_rn(c, B[j]);
         B[j] = c;
       }
     } else {
-      for (int j = 0; j < count; ++j) c = __fadd_rn(c, B[j]);
+      for (int q = 0; q < n4; ++q) {
+        const float4 v = B4[q];
+        c = __fadd_rn(c, v.x);
+        c = __fadd_rn(c, v.y);
+        c = __fadd_rn(c, v.z);
+        c = __fadd_rn(c, v.w);
+      }
+      for (int j = n4 << 2; j < count; ++j) c = __fadd_rn(c, B[j]);
     }
   }
   __syncwarp();
@@ -401,6 +448,125 @@ struct DebugRow {
   float* probs;
 };
 
+// Top-p over a survivor list in vocabulary order (sampling.rs:665-698): the
+// full-vocabulary softmax denominator, the max - 16 cutoff and the nucleus
+// walked in (p desc, index asc) order.  On return the list holds the nucleus
+// (in vocabulary order, B = exp(x - m2)), *ns_io its length, *m2_out its max.
+// Kept out of line: only rows with top_p < 1 execute it.
+__device__ __noinline__ int apply_top_p(float* B, float* BX, uint16_t* BI, int* ns_io, float m1,
+                                        double top_p_d, unsigned long long* keys, uint32_t* hist,
+                                        float* m2_out) {
+  const unsigned lane = lane_id();
+  const int ns = *ns_io;
+  // Denominator: sequential f32 sum in vocabulary order.
+  const float total = chain_sum(B, ns, false);
+  if (!is_finite(total) || total <= 0.0f) return Q3S_STATUS_INVALID_DENOMINATOR;
+  const float inv_total = __fdiv_rn(1.0f, total);
+  const float cutoff = __fsub_rn(m1, 16.0f);
+  int np = 0;
+  for (int j = lane; j < ns; j += 32) {
+    const float p = BX[j] >= cutoff ? __fmul_rn(B[j], inv_total) : 0.0f;
+    B[j] = p;
+    np += p > 0.0f ? 1 : 0;
+  }
+  np = __reduce_add_sync(FULL, np);
+  __syncwarp();
+  // Walk the probabilities in (p desc, index asc) order, 256 at a time; the
+  // first position > 0 whose preceding cumulative reaches top_p starts the
+  // masked tail.
+  const float top_p = (float)top_p_d;
+  float cum = 0.0f;
+  int pos = 0;
+  unsigned long long cut = ~0ull, last = 0ull;
+  int remaining = np;
+  auto pkey = [&](int j, unsigned long long& k) {
+    const float p = B[j];
+    k = nucleus_key(p, BI[j]);
+    return p > 0.0f && k > last;
+  };
+#pragma unroll 1
+  while (remaining > 0) {
+    const int m = remaining < 256 ? remaining : 256;
+    unsigned long long hi = ~0ull;
+    if (remaining > 256) hi = warp_select<unsigned long long>(ns, 256u, pkey, hist, 56);
+    int cnt = 0;
+    for (int j0 = 0; j0 < ns; j0 += 32) {
+      const int j = j0 + lane;
+      unsigned long long k = 0;
+      const bool p = j < ns && pkey(j, k) && k <= hi;
+      const unsigned b = __ballot_sync(FULL, p);
+      if (p) {
+        const int d = cnt + __popc(b & lanemask_lt());
+        if (d < 256) keys[d] = k;
+      }
+      cnt += __popc(b);
+    }
+    if (cnt > 256) cnt = 256;
+    __syncwarp();
+    unsigned long long v[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int e = lane * 8 + r;
+      v[r] = e < cnt ? keys[e] : ~0ull;
+    }
+    __syncwarp();
+    bitonic_sort_256(v);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) keys[lane * 8 + r] = v[r];
+    __syncwarp();
+    if (lane == 0) {
+      for (int q = 0; q < cnt; ++q) {
+        const unsigned long long k = keys[q];
+        const float p = __uint_as_float(~(uint32_t)(k >> 32));
+        if (pos > 0 && cum >= top_p) {
+          cut = k;
+          break;
+        }
+        cum = __fadd_rn(cum, p);
+        ++pos;
+      }
+    }
+    cut = __shfl_sync(FULL, cut, 0);
+    cum = __shfl_sync(FULL, cum, 0);
+    pos = __shfl_sync(FULL, pos, 0);
+    __syncwarp();
+    if (cut != ~0ull) break;
+    last = hi;
+    remaining -= m;
+  }
+  // Final survivors: nucleus members before the cut.
+  float m2 = neg_inf();
+  for (int j = lane; j < ns; j += 32) {
+    const float p = B[j];
+    if (p > 0.0f && nucleus_key(p, BI[j]) >= cut) B[j] = 0.0f;
+    if (B[j] > 0.0f) m2 = fmaxf(m2, BX[j]);
+  }
+  m2 = warp_max(m2);
+  __syncwarp();
+  if (!(m2 > neg_inf())) return Q3S_STATUS_NO_CANDIDATE;
+  // Compact the survivors in place with the final softmax numerators.
+  int ns2 = 0;
+  for (int j0 = 0; j0 < ns; j0 += 32) {
+    const int j = j0 + lane;
+    const bool p = j < ns && B[j] > 0.0f;
+    const int i = p ? BI[j] : 0;
+    const float x = p ? BX[j] : 0.0f;
+    __syncwarp();
+    const unsigned b = __ballot_sync(FULL, p);
+    if (p) {
+      const int d = ns2 + __popc(b & lanemask_lt());
+      BI[d] = (uint16_t)i;
+      BX[d] = x;
+      B[d] = cr_expf(__fsub_rn(x, m2));
+    }
+    ns2 += __popc(b);
+    __syncwarp();
+  }
+  *ns_io = ns2;
+  *m2_out = m2;
+  return Q3S_STATUS_OK;
+}
+
 // Top-p, final softmax and draw over a survivor list in vocabulary order:
 // B[j] = exp(x_j - m1), BX[j] = x_j, BI[j] = index, m1 = max x (sampling.rs:665-729).
 __device__ RowOut finish_list(float* B, float* BX, uint16_t* BI, int ns, float m1,
@@ -409,111 +575,8 @@ __device__ RowOut finish_list(float* B, float* BX, uint16_t* BI, int ns, float m
   const unsigned lane = lane_id();
   float m2 = m1;
   if (P.top_p < 1.0) {
-    // Denominator: sequential f32 sum in vocabulary order.
-    const float total = chain_sum(B, ns, false);
-    if (!is_finite(total) || total <= 0.0f) return {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
-    const float inv_total = __fdiv_rn(1.0f, total);
-    const float cutoff = __fsub_rn(m1, 16.0f);
-    int np = 0;
-    for (int j = lane; j < ns; j += 32) {
-      const float p = BX[j] >= cutoff ? __fmul_rn(B[j], inv_total) : 0.0f;
-      B[j] = p;
-      np += p > 0.0f ? 1 : 0;
-    }
-    np = __reduce_add_sync(FULL, np);
-    __syncwarp();
-    // Walk the probabilities in (p desc, index asc) order, 256 at a time; the
-    // first position > 0 whose preceding cumulative reaches top_p starts the
-    // masked tail.
-    const float top_p = (float)P.top_p;
-    float cum = 0.0f;
-    int pos = 0;
-    unsigned long long cut = ~0ull, last = 0ull;
-    int remaining = np;
-    auto pkey = [&](int j, unsigned long long& k) {
-      const float p = B[j];
-      k = nucleus_key(p, BI[j]);
-      return p > 0.0f && k > last;
-    };
-#pragma unroll 1
-    while (remaining > 0) {
-      const int m = remaining < 256 ? remaining : 256;
-      unsigned long long hi = ~0ull;
-      if (remaining > 256) hi = warp_select<unsigned long long>(ns, 256u, pkey, hist, 56);
-      int cnt = 0;
-      for (int j0 = 0; j0 < ns; j0 += 32) {
-        const int j = j0 + lane;
-        unsigned long long k = 0;
-        const bool p = j < ns && pkey(j, k) && k <= hi;
-        const unsigned b = __ballot_sync(FULL, p);
-        if (p) {
-          const int d = cnt + __popc(b & lanemask_lt());
-          if (d < 256) keys[d] = k;
-        }
-        cnt += __popc(b);
-      }
-      if (cnt > 256) cnt = 256;
-      __syncwarp();
-      unsigned long long v[8];
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const int e = lane * 8 + r;
-        v[r] = e < cnt ? keys[e] : ~0ull;
-      }
-      __syncwarp();
-      bitonic_sort_256(v);
-#pragma unroll
-      for (int r = 0; r < 8; ++r) keys[lane * 8 + r] = v[r];
-      __syncwarp();
-      if (lane == 0) {
-        for (int q = 0; q < cnt; ++q) {
-          const unsigned long long k = keys[q];
-          const float p = __uint_as_float(~(uint32_t)(k >> 32));
-          if (pos > 0 && cum >= top_p) {
-            cut = k;
-            break;
-          }
-          cum = __fadd_rn(cum, p);
-          ++pos;
-        }
-      }
-      cut = __shfl_sync(FULL, cut, 0);
-      cum = __shfl_sync(FULL, cum, 0);
-      pos = __shfl_sync(FULL, pos, 0);
-      __syncwarp();
-      if (cut != ~0ull) break;
-      last = hi;
-      remaining -= m;
-    }
-    // Final survivors: nucleus members before the cut.
-    m2 = neg_inf();
-    for (int j = lane; j < ns; j += 32) {
-      const float p = B[j];
-      if (p > 0.0f && nucleus_key(p, BI[j]) >= cut) B[j] = 0.0f;
-      if (B[j] > 0.0f) m2 = fmaxf(m2, BX[j]);
-    }
-    m2 = warp_max(m2);
-    __syncwarp();
-    if (!(m2 > neg_inf())) return {Q3S_STATUS_NO_CANDIDATE, 0u};
-    // Compact the survivors in place with the final softmax numerators.
-    int ns2 = 0;
-    for (int j0 = 0; j0 < ns; j0 += 32) {
-      const int j = j0 + lane;
-      const bool p = j < ns && B[j] > 0.0f;
-      const int i = p ? BI[j] : 0;
-      const float x = p ? BX[j] : 0.0f;
-      __syncwarp();
-      const unsigned b = __ballot_sync(FULL, p);
-      if (p) {
-        const int d = ns2 + __popc(b & lanemask_lt());
-        BI[d] = (uint16_t)i;
-        BX[d] = x;
-        B[d] = cr_expf(__fsub_rn(x, m2));
-      }
-      ns2 += __popc(b);
-      __syncwarp();
-    }
-    ns = ns2;
+    const int st = apply_top_p(B, BX, BI, &ns, m1, P.top_p, keys, hist, &m2);
+    if (st != Q3S_STATUS_OK) return {st, 0u};
   }
 
   // Final softmax sum and the draw (sampling.rs:700-729).
@@ -593,7 +656,7 @@ __device__ RowOut greedy_stage(const FastSpace& f, const StageView& s, int sf, i
 // General path: the full row as f32 in the global workspace, then full-row
 // passes (any top_k, any temperature).
 template <int DT>
-__device__ RowOut general_row(const FastSpace& f, const GenSpace& g, const StageView& s,
+__device__ __noinline__ RowOut general_row(const FastSpace& f, const GenSpace& g, const StageView& s,
                               const q3s_row_params& P, const RowCtx& rc, float u, Releaser& rel,
                               const DebugRow& dbg) {
   const unsigned lane = lane_id();
@@ -687,46 +750,136 @@ __device__ __forceinline__ int count_ge(const float (&vm)[NJ], float tau) {
   return (int)__reduce_add_sync(FULL, (unsigned)c);
 }
 
-// Candidates {x >= tau} of the flagged vectors into f.cand (x after the
-// temperature, index); returns their count (may exceed CAP: overflow).
+// Candidates {x >= tau} of the flagged vectors, each lane into its own slots
+// of f.cand (slot t of lane l at t*32 + l: conflict-free), as (x after the
+// temperature, index).  Returns this lane's count (above SEG: overflow).
 template <int DT, int NJ, bool XF, bool EDGE>
 __device__ int collect(const FastSpace& f, const RowCtx& r, const float (&vm)[NJ], float tau) {
   constexpr int EPV = Elem<DT>::EPV;
   const int lane = (int)lane_id();
-  if (lane == 0) *f.counter = 0u;
-  __syncwarp();
   uint64_t flags = 0;
 #pragma unroll
   for (int j = 0; j < NJ; ++j) flags |= (vm[j] >= tau ? 1ull : 0ull) << j;
+  int cnt = 0;
   while (flags) {
     const int j = __ffsll((long long)flags) - 1;
     flags &= flags - 1;
     const int q = lane + 32 * j;
     float e[EPV];
     unpack<DT>(f.stage, q, e);
-    float x[EPV];
-    int cnt = 0;
 #pragma unroll
     for (int c = 0; c < EPV; ++c) {
-      x[c] = xform<XF, EDGE>(e[c], q * EPV + c - r.mis, r);
-      cnt += x[c] >= tau ? 1 : 0;
-    }
-    uint32_t pos = atomicAdd(f.counter, (uint32_t)cnt);
-#pragma unroll
-    for (int c = 0; c < EPV; ++c) {
-      if (x[c] >= tau) {
-        if (pos < (uint32_t)CAP) {
-          const float xv = XF ? x[c] : __fmul_rn(x[c], r.inv);
-          f.cand[pos] = make_uint2(__float_as_uint(xv), (uint32_t)(q * EPV + c - r.mis));
+      const float x = xform<XF, EDGE>(e[c], q * EPV + c - r.mis, r);
+      if (x >= tau) {
+        if (cnt < SEG) {
+          const float xv = XF ? x : __fmul_rn(x, r.inv);
+          f.cand[cnt * 32 + lane] = make_uint2(__float_as_uint(xv), (uint32_t)(q * EPV + c - r.mis));
         }
-        ++pos;
+        ++cnt;
       }
     }
   }
   __syncwarp();
-  const int c = (int)*f.counter;
-  __syncwarp();
-  return c;
+  return cnt;
+}
+
+// Exact k-th largest x among the candidates (each lane holds `mine` of
+// them).  Bins of equal width over the current value range, counted from the
+// top; the range narrows to the bin that holds the k-th value until that bin
+// holds one value (or one distinct value).  The bin function
+// floor((x - lo) * scale) is monotone in x, so the bins partition the
+// candidates in value order.
+__device__ float select_kth_candidate(const FastSpace& f, int mine, int k) {
+  const unsigned lane = lane_id();
+  float lo = __int_as_float(0x7f800000), hi = neg_inf();
+  for (int t = 0; t < mine; ++t) {
+    const float x = __uint_as_float(f.cand[t * 32 + lane].x);
+    lo = fminf(lo, x);
+    hi = fmaxf(hi, x);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = fminf(lo, __shfl_xor_sync(FULL, lo, o));
+    hi = fmaxf(hi, __shfl_xor_sync(FULL, hi, o));
+  }
+  uint32_t kk = (uint32_t)k;
+#pragma unroll 1
+  for (int pass = 0; pass < 8; ++pass) {
+    if (!(hi > lo)) return hi;  // one distinct value left
+    const float width = __fsub_rn(hi, lo);
+    if (!(width < __int_as_float(0x7f800000))) break;  // range too wide: key radix below
+    const float scale = __fdiv_rn(63.5f, width);
+    // 64 bins, counted in f.hist.
+    f.hist[lane] = 0u;
+    f.hist[lane + 32] = 0u;
+    __syncwarp();
+    for (int t = 0; t < mine; ++t) {
+      const float x = __uint_as_float(f.cand[t * 32 + lane].x);
+      if (x >= lo && x <= hi) {
+        const int b = min(63, (int)__fmul_rn(__fsub_rn(x, lo), scale));
+        atomicAdd(&f.hist[b], 1u);
+      }
+    }
+    __syncwarp();
+    // Lane l owns bins 63-2l and 62-2l (counted from the top).
+    const uint32_t c0 = f.hist[63 - 2 * lane], c1 = f.hist[62 - 2 * lane];
+    const uint32_t s = c0 + c1;
+    const uint32_t incl = warp_inclusive_scan(s);
+    const unsigned ball = __ballot_sync(FULL, incl >= kk);
+    const int src = ball ? __ffs(ball) - 1 : 31;
+    int bin = 0;
+    uint32_t before = 0, inbin = 0;
+    if ((int)lane == src) {
+      const uint32_t acc = incl - s;
+      if (acc + c0 >= kk) {
+        bin = 63 - 2 * lane;
+        before = acc;
+        inbin = c0;
+      } else {
+        bin = 62 - 2 * lane;
+        before = acc + c0;
+        inbin = c1;
+      }
+    }
+    bin = __shfl_sync(FULL, bin, src);
+    before = __shfl_sync(FULL, before, src);
+    inbin = __shfl_sync(FULL, inbin, src);
+    kk -= before;
+    // Value range of the chosen bin.
+    float nlo = __int_as_float(0x7f800000), nhi = neg_inf();
+    for (int t = 0; t < mine; ++t) {
+      const float x = __uint_as_float(f.cand[t * 32 + lane].x);
+      if (x >= lo && x <= hi && min(63, (int)__fmul_rn(__fsub_rn(x, lo), scale)) == bin) {
+        nlo = fminf(nlo, x);
+        nhi = fmaxf(nhi, x);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      nlo = fminf(nlo, __shfl_xor_sync(FULL, nlo, o));
+      nhi = fmaxf(nhi, __shfl_xor_sync(FULL, nhi, o));
+    }
+    lo = nlo;
+    hi = nhi;
+    if (inbin == 1u) return hi;
+    __syncwarp();
+  }
+  // Fallback: radix selection on total-order keys below the current range.
+  const uint32_t kmax = total_key(hi);
+  const uint32_t kspan = kmax - total_key(lo);
+  const int bits = 32 - __clz(kspan | 1u);
+  const int top = ((bits + 7) / 8) * 8 - 8;
+  const float flo = lo, fhi = hi;
+  // warp_select visits slot j = t*32 + lane from lane `lane`: its own slots.
+  const uint32_t rel_k = warp_select<uint32_t>(
+      32 * SEG, kk,
+      [&](int j, uint32_t& key) {
+        const float x = __uint_as_float(f.cand[j].x);
+        key = kmax - total_key(x);
+        return (j >> 5) < mine && x >= flo && x <= fhi;
+      },
+      f.hist, top);
+  return from_total_key(kmax - rel_k);
 }
 
 // Debug pass over the stage: bit0 finite x, bit1 x >= t.
@@ -818,59 +971,42 @@ __device__ bool fast_row(const FastSpace& f, const StageView& s, const q3s_row_p
     if (!ok) return false;
     tau = t2;
   }
-  const int c = collect<DT, NJ, XF, EDGE>(f, rc, vm, tau);
-  if (c > CAP || c < k) return false;
+  const int mine = collect<DT, NJ, XF, EDGE>(f, rc, vm, tau);
+  const bool overflow = __any_sync(FULL, mine > SEG);
+  const int c = (int)__reduce_add_sync(FULL, (unsigned)mine);
+  // The survivors (at most c) must fit the list; decided before release.
+  if (overflow || c < k || c > LCAP) return false;
   delta = d;
   if (!dbg.masks) release<DT>(rel);
 
-  // Exact k-th largest candidate: keys relative to the largest key.
-  uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
-  for (int j = lane; j < c; j += 32) {
-    const uint32_t kk = total_key(__uint_as_float(f.cand[j].x));
-    kmin = min(kmin, kk);
-    kmax = max(kmax, kk);
-  }
-  kmin = __reduce_min_sync(FULL, kmin);
-  kmax = __reduce_max_sync(FULL, kmax);
-  const uint32_t kspan = kmax - kmin;
-  float t;
-  if (kspan == 0u) {
-    t = from_total_key(kmax);
-  } else {
-    const int bits = 32 - __clz(kspan);
-    const int top = ((bits + 7) / 8) * 8 - 8;
-    const uint32_t rel_k = warp_select<uint32_t>(
-        c, (uint32_t)k,
-        [&](int j, uint32_t& key) {
-          key = kmax - total_key(__uint_as_float(f.cand[j].x));
-          return true;
-        },
-        f.hist, top);
-    t = from_total_key(kmax - rel_k);
-  }
+  // Exact k-th largest candidate.
+  const float t = select_kth_candidate(f, mine, k);
+  // The debug masks recompute x with the history bitmap, which the survivor
+  // bitmap below overwrites.
+  if (dbg.masks) debug_masks<DT, XF>(f, rc, t, dbg.masks);
   // Survivors x >= t, in vocabulary order through a bitmap.
   const int words = (n + 31) >> 5;
   for (int w = lane; w < words; w += 32) f.bm[w] = 0u;
   __syncwarp();
-  for (int j = lane; j < c; j += 32) {
-    const uint2 e = f.cand[j];
+  for (int s = 0; s < mine; ++s) {
+    const uint2 e = f.cand[s * 32 + lane];
     if (__uint_as_float(e.x) >= t) atomicOr(&f.bm[e.y >> 5], 1u << (e.y & 31));
   }
   __syncwarp();
   const int per = (words + 31) >> 5;
   const int w0 = min(words, (int)lane * per), w1 = min(words, w0 + per);
-  int mine = 0;
-  for (int w = w0; w < w1; ++w) mine += __popc(f.bm[w]);
-  const int incl = (int)warp_inclusive_scan((uint32_t)mine);
-  int run = incl - mine;
+  int own = 0;
+  for (int w = w0; w < w1; ++w) own += __popc(f.bm[w]);
+  const int incl = (int)warp_inclusive_scan((uint32_t)own);
+  int run = incl - own;
   for (int w = w0; w < w1; ++w) {
     f.wpre[w] = (uint16_t)run;
     run += __popc(f.bm[w]);
   }
   const int ns = __shfl_sync(FULL, incl, 31);
   __syncwarp();
-  for (int j = lane; j < c; j += 32) {
-    const uint2 e = f.cand[j];
+  for (int s = 0; s < mine; ++s) {
+    const uint2 e = f.cand[s * 32 + lane];
     const float x = __uint_as_float(e.x);
     if (x >= t) {
       const uint32_t w = e.y >> 5, b = e.y & 31;
@@ -881,7 +1017,6 @@ __device__ bool fast_row(const FastSpace& f, const StageView& s, const q3s_row_p
     }
   }
   __syncwarp();
-  if (dbg.masks) debug_masks<DT, XF>(f, rc, t, dbg.masks);
   out = finish_list(f.B, f.BX, f.BI, ns, Mx, P, reinterpret_cast<unsigned long long*>(f.cand),
                     f.hist, u, n, dbg);
   release<DT>(rel);
@@ -890,8 +1025,9 @@ __device__ bool fast_row(const FastSpace& f, const StageView& s, const q3s_row_p
 
 template <int DT, int NJ>
 __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const GenSpace& g,
-                              long long row, const StageView& s, const q3s_row_params& P,
-                              Releaser& rel, float& delta, const DebugRow& dbg) {
+                              const RowMeta& m, const StageView& s, Releaser& rel, float& delta,
+                              const DebugRow& dbg) {
+  const q3s_row_params& P = m.P;
   RowCtx rc;
   rc.n = s.n;
   rc.mis = s.mis;
@@ -901,14 +1037,8 @@ __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const Gen
   rc.sf = P.suppress_from;
   rc.allow = P.allow_token;
   rc.bm = f.bm;
-  long long h0 = 0, h1 = 0;
-  if (a.history_offsets) {
-    h0 = a.history_offsets[row];
-    h1 = a.history_offsets[row + 1];
-  }
-  rc.use_pen = P.repetition_penalty != 1.0 && h1 > h0;
-  const float u = a.uniform_override ? a.uniform_override[row]
-                                     : philox_uniform(a.seeds[row], a.subseqs[row], P.ctr_lo);
+  rc.use_pen = P.repetition_penalty != 1.0 && m.h1 > m.h0;
+  const float u = a.uniform_override ? m.uo : philox_uniform(m.seed, m.subseq, P.ctr_lo);
   const bool inv_ok = rc.inv > 0.0f && rc.inv < __int_as_float(0x7f800000);
   const bool fast = inv_ok && P.top_k >= 1u && P.top_k <= (uint32_t)FAST_MAX_K &&
                     P.top_k < (uint32_t)s.n;
@@ -949,10 +1079,15 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
   if (row < a.num_rows && lane == 0) issue_row<DT>(a, row, f);
   uint32_t phase = 0;
   float delta = 0.0f;
+  // Per-row metadata is loaded one row ahead so its latency overlaps a row.
+  RowMeta cur;
+  if (row < a.num_rows) cur = load_meta(a, row);
   for (; row < a.num_rows; row += stride) {
     Releaser rel{&a, &f, row + stride, false};
-    const int n = row_vocab(a, row);
-    const q3s_row_params P = a.params[row * a.params_stride];
+    RowMeta nxt;
+    if (row + stride < a.num_rows) nxt = load_meta(a, row + stride);
+    const int n = cur.n;
+    const q3s_row_params& P = cur.P;
     int st = row_fits(a, n) ? validate(P) : Q3S_STATUS_UNSUPPORTED;
     DebugRow dbg{nullptr, nullptr};
     if (a.masks && st == Q3S_STATUS_OK) dbg.masks = a.masks + row * a.probs_stride;
@@ -963,8 +1098,8 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
       for (int i = lane; i < n; i += 32) dbg.probs[i] = 0.0f;
     // History bitmap of a sampled row with a penalty (filled while the
     // stage copy is in flight).
-    if (st == Q3S_STATUS_OK && P.do_sample && P.repetition_penalty != 1.0 && a.history_offsets) {
-      const long long h0 = a.history_offsets[row], h1 = a.history_offsets[row + 1];
+    if (st == Q3S_STATUS_OK && P.do_sample && P.repetition_penalty != 1.0) {
+      const long long h0 = cur.h0, h1 = cur.h1;
       if (h1 > h0) {
         const int words = (n + 31) >> 5;
         for (int w = lane; w < words; w += 32) f.bm[w] = 0u;
@@ -996,7 +1131,7 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
         out = greedy_stage<DT>(f, s, P.suppress_from, P.allow_token);
         release<DT>(rel);
       } else {
-        out = sampled_row<DT, NJ>(a, f, g, row, s, P, rel, delta, dbg);
+        out = sampled_row<DT, NJ>(a, f, g, cur, s, rel, delta, dbg);
       }
     }
     release<DT>(rel);
@@ -1005,6 +1140,7 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
       a.status[row] = (unsigned char)out.status;
     }
     __syncwarp();
+    cur = nxt;
   }
 }
 
