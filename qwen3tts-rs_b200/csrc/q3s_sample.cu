@@ -1,12 +1,11 @@
 // Fused per-step sampling kernel for the Qwen3-TTS talker / code predictor.
 //
-// One warp samples one row: repetition penalty over the row's history
-// (sampling.rs:592-606, 732-773), suppression / non-finite mask (:608-616),
-// temperature as a reciprocal multiply (:628-631), top-k keeping every tie of
-// the k-th value (:633-663), top-p over the full-vocabulary softmax (:665-698)
-// and the vocabulary-order multinomial draw with Philox4x32-10 (:700-729,
-// :337-375).  Greedy rows take the total_cmp argmax of the raw logits
-// (:574-591).
+// Per row: repetition penalty over the row's history (sampling.rs:592-606,
+// 732-773), suppression / non-finite mask (:608-616), temperature as a
+// reciprocal multiply (:628-631), top-k keeping every tie of the k-th value
+// (:633-663), top-p over the full-vocabulary softmax (:665-698) and the
+// vocabulary-order multinomial draw with Philox4x32-10 (:700-729, :337-375).
+// Greedy rows take the total_cmp argmax of the raw logits (:574-591).
 //
 // Exactness: every f32 operation of the reference is performed with the same
 // rounding, and every f32 running sum the reference accumulates sequentially
@@ -14,27 +13,30 @@
 // the draw's cumulative) is accumulated sequentially here too, over the same
 // non-zero terms in the same order.  Terms the reference adds that are exact
 // zeros (exp(-inf)) are skipped, which leaves an f32 sum unchanged.  The
-// parallel parts (max, counts, selection, sorting) are order-free.
+// order-free parts (maxima, counts, selection, sorting) are parallel.
 //
-// Data movement: a persistent grid of warps strides over rows.  Each warp
-// owns one shared-memory stage; its next row is fetched by a bulk copy (TMA,
-// cp.async.bulk, no multicast) that completes on the warp's mbarrier while the
-// warp finishes the current row.  The row is read from the stage once in the
-// common case (the "fast path"):
-//   1. one scan of the stage computes every 16-byte vector's maximum (kept in
-//      registers) and the row maximum;
-//   2. a threshold tau is chosen on the vector maxima so that at least k
-//      vectors (hence at least k elements) reach it: the candidates
-//      {x >= tau} then contain the whole top-k set, ties included;
-//   3. only the vectors whose maximum reaches tau are re-read to collect the
-//      candidates (a few hundred of the row's thousands of elements); the
-//      stage is then released to the next row's copy;
-//   4. the exact k-th largest candidate is found by radix selection, the
-//      survivors are put in vocabulary order through a bitmap, and the
-//      softmax / top-p / draw run on that short list.
+// Data movement and work split.  A persistent grid of warps strides over the
+// rows.  Each warp owns one shared-memory stage; its next row arrives by a
+// bulk copy (TMA, cp.async.bulk, no multicast) completing on the warp's
+// mbarrier while the warp works on the current row.  Common rows take the
+// fast path:
+//   1. the warp scans the stage once, keeping each 16-byte vector's maximum
+//      in registers, and reduces the row maximum;
+//   2. it picks a threshold tau on the vector maxima such that at least k
+//      vectors (hence at least k elements) reach it, so the candidates
+//      {x >= tau} contain the whole top-k set, ties included;
+//   3. it re-reads only the vectors whose maximum reaches tau and appends
+//      their candidates (a few dozen to a few hundred per row) to a per-warp
+//      arena, then releases the stage to the next row's copy;
+//   4. once 32 rows are pending (or the arena is full), each lane finishes
+//      one row from its candidate list: exact k-th largest by quickselect,
+//      survivors sorted into vocabulary order, top-p and the draw.  The
+//      sequential sums are sequential per lane anyway, and 32 rows proceed
+//      in parallel without warp-level synchronisation.
 // Rows outside the fast path (top_k off or above 256, a temperature whose
-// reciprocal is 0 or infinite, a candidate overflow) run the same algorithm
-// on full-row lists kept in a per-warp global workspace ("general path").
+// reciprocal is 0 or infinite, too many candidates, +inf logits) run the
+// same algorithm warp-cooperatively on full-row lists kept in a per-warp
+// global workspace ("general path").
 
 #include <cstdint>
 
@@ -45,10 +47,10 @@
 namespace q3s {
 namespace {
 
-constexpr int MAX_WARPS = 10;
-constexpr int SEG = 24;         // candidate slots per lane (interleaved: slot t of lane l at t*32+l)
-constexpr int CAP = 32 * SEG;   // fast-path candidate capacity per warp
-constexpr int LCAP = 512;       // fast-path survivor-list capacity per warp
+constexpr int MAX_WARPS = 8;
+constexpr int ARENA = 1536;       // candidate entries per warp (8 bytes each)
+constexpr int ROW_CAP = 768;      // candidates one fast row may hold
+constexpr int MAX_SLOTS = 32;     // pending rows per warp (one per lane)
 constexpr int FAST_MAX_K = 256;
 constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;  // bounded wait for a stage: 1 s
 
@@ -69,23 +71,30 @@ __host__ __device__ inline size_t stage_bytes(int vcap, int es) {
   return align16((size_t)vcap * es + 16);
 }
 
-// Per-warp shared memory of the fast path.
+// A pending fast row: its candidates are arena[off, off + c) as (x bits,
+// index); rows with top-p also own c floats after them.
+struct Slot {
+  long long row;
+  int off, c, k, n;
+  float Mx;      // row maximum of x
+  float u;       // the row's uniform draw
+  float top_p;   // top_p as f32
+  int use_top_p; // top_p < 1.0 (f64 comparison)
+};
+
+// Per-warp shared memory.
 struct FastSpace {
-  unsigned char* stage;        // raw row, TMA destination
-  uint2* cand;                 // [CAP] (x bits, index); the nucleus sort aliases it
-  float* B;                    // [LCAP] softmax numerators of the survivor list
-  float* BX;                   // [LCAP] x of the survivor list
-  uint16_t* BI;                // [LCAP] vocabulary index of the survivor list
-  uint32_t* bm;                // [vcap/32] history bitmap, then survivor bitmap
-  uint16_t* wpre;              // [vcap/32] survivors before each bitmap word
-  uint32_t* hist;              // [256]
-  uint64_t* mbar;              // stage barrier
-  uint32_t* counter;           // candidate slot counter
+  unsigned char* stage;  // raw row, TMA destination
+  uint2* arena;          // [ARENA]; the general path uses it as sort space
+  Slot* slots;           // [MAX_SLOTS]
+  uint32_t* bm;          // [vcap/32] history bitmap
+  uint32_t* hist;        // [256]
+  uint64_t* mbar;        // stage barrier
 };
 
 __host__ __device__ inline size_t fast_bytes(int vcap, int es) {
-  return stage_bytes(vcap, es) + 8u * CAP + 4u * LCAP * 2 + align16(2u * LCAP) +
-         align16(4u * (vcap / 32)) + align16(2u * (vcap / 32)) + 4u * 256 + 16u;
+  return stage_bytes(vcap, es) + 8u * ARENA + align16(sizeof(Slot) * MAX_SLOTS) +
+         align16(4u * (vcap / 32)) + 4u * 256 + 16u;
 }
 
 __device__ inline FastSpace carve_fast(unsigned char* base, int vcap, int es) {
@@ -93,22 +102,15 @@ __device__ inline FastSpace carve_fast(unsigned char* base, int vcap, int es) {
   size_t o = 0;
   f.stage = base;
   o += stage_bytes(vcap, es);
-  f.cand = reinterpret_cast<uint2*>(base + o);
-  o += 8u * CAP;
-  f.B = reinterpret_cast<float*>(base + o);
-  o += 4u * LCAP;
-  f.BX = reinterpret_cast<float*>(base + o);
-  o += 4u * LCAP;
-  f.BI = reinterpret_cast<uint16_t*>(base + o);
-  o += align16(2u * LCAP);
+  f.arena = reinterpret_cast<uint2*>(base + o);
+  o += 8u * ARENA;
+  f.slots = reinterpret_cast<Slot*>(base + o);
+  o += align16(sizeof(Slot) * MAX_SLOTS);
   f.bm = reinterpret_cast<uint32_t*>(base + o);
   o += align16(4u * (vcap / 32));
-  f.wpre = reinterpret_cast<uint16_t*>(base + o);
-  o += align16(2u * (vcap / 32));
   f.hist = reinterpret_cast<uint32_t*>(base + o);
   o += 4u * 256;
   f.mbar = reinterpret_cast<uint64_t*>(base + o);
-  f.counter = reinterpret_cast<uint32_t*>(base + o + 8);
   return f;
 }
 
@@ -138,7 +140,7 @@ struct RowOut {
   uint32_t token;
 };
 
-// Where row r's elements sit in the stage: element i at byte mis*es + i*es.
+// Where a row's elements sit in the stage: element i at byte (mis + i) * es.
 struct StageView {
   int n;    // elements
   int mis;  // leading misalignment in elements
@@ -313,6 +315,16 @@ __device__ __forceinline__ float xform(float v, int i, const RowCtx& r) {
   return __fmul_rn(v, r.inv);
 }
 
+// Debug outputs of one row (probs and masks), NULL when not requested.
+struct DebugRow {
+  unsigned char* masks;
+  float* probs;
+};
+
+// ===========================================================================
+// General path (warp-cooperative over full-row lists).
+// ===========================================================================
+
 // k-th smallest (1-based) key among the valid elements, MSB-first radix
 // selection with 8-bit digits from bit `top_shift + 8` down.  Requires at
 // least k valid elements whose keys are below 2^(top_shift + 8).
@@ -442,25 +454,24 @@ __device__ __forceinline__ unsigned long long nucleus_key(float p, uint16_t idx)
   return ((unsigned long long)(~__float_as_uint(p)) << 32) | idx;
 }
 
-// Debug outputs of one row (probs and masks), NULL when not requested.
-struct DebugRow {
-  unsigned char* masks;
-  float* probs;
-};
+__device__ __forceinline__ unsigned long long pack_top_p(int status, int ns, float m2) {
+  return ((unsigned long long)(unsigned)status << 56) | ((unsigned long long)(unsigned)ns << 32) |
+         __float_as_uint(m2);
+}
 
 // Top-p over a survivor list in vocabulary order (sampling.rs:665-698): the
 // full-vocabulary softmax denominator, the max - 16 cutoff and the nucleus
-// walked in (p desc, index asc) order.  On return the list holds the nucleus
-// (in vocabulary order, B = exp(x - m2)), *ns_io its length, *m2_out its max.
-// Kept out of line: only rows with top_p < 1 execute it.
-__device__ __noinline__ int apply_top_p(float* B, float* BX, uint16_t* BI, int* ns_io, float m1,
-                                        double top_p_d, unsigned long long* keys, uint32_t* hist,
-                                        float* m2_out) {
+// walked in (p desc, index asc) order, 256 at a time.  On return the list
+// holds the nucleus (vocabulary order, B = exp(x - m2)).  Returns status,
+// nucleus length and m2 packed by pack_top_p.
+__device__ unsigned long long apply_top_p(float* B, float* BX, uint16_t* BI, int ns, float m1,
+                                          double top_p_d, unsigned long long* keys,
+                                          uint32_t* hist) {
   const unsigned lane = lane_id();
-  const int ns = *ns_io;
   // Denominator: sequential f32 sum in vocabulary order.
   const float total = chain_sum(B, ns, false);
-  if (!is_finite(total) || total <= 0.0f) return Q3S_STATUS_INVALID_DENOMINATOR;
+  if (!is_finite(total) || total <= 0.0f)
+    return pack_top_p(Q3S_STATUS_INVALID_DENOMINATOR, 0, 0.0f);
   const float inv_total = __fdiv_rn(1.0f, total);
   const float cutoff = __fsub_rn(m1, 16.0f);
   int np = 0;
@@ -471,9 +482,8 @@ __device__ __noinline__ int apply_top_p(float* B, float* BX, uint16_t* BI, int* 
   }
   np = __reduce_add_sync(FULL, np);
   __syncwarp();
-  // Walk the probabilities in (p desc, index asc) order, 256 at a time; the
-  // first position > 0 whose preceding cumulative reaches top_p starts the
-  // masked tail.
+  // The first position > 0 whose preceding cumulative reaches top_p starts
+  // the masked tail.
   const float top_p = (float)top_p_d;
   float cum = 0.0f;
   int pos = 0;
@@ -543,7 +553,7 @@ __device__ __noinline__ int apply_top_p(float* B, float* BX, uint16_t* BI, int* 
   }
   m2 = warp_max(m2);
   __syncwarp();
-  if (!(m2 > neg_inf())) return Q3S_STATUS_NO_CANDIDATE;
+  if (!(m2 > neg_inf())) return pack_top_p(Q3S_STATUS_NO_CANDIDATE, 0, 0.0f);
   // Compact the survivors in place with the final softmax numerators.
   int ns2 = 0;
   for (int j0 = 0; j0 < ns; j0 += 32) {
@@ -562,55 +572,132 @@ __device__ __noinline__ int apply_top_p(float* B, float* BX, uint16_t* BI, int* 
     ns2 += __popc(b);
     __syncwarp();
   }
-  *ns_io = ns2;
-  *m2_out = m2;
-  return Q3S_STATUS_OK;
+  return pack_top_p(Q3S_STATUS_OK, ns2, m2);
 }
 
-// Top-p, final softmax and draw over a survivor list in vocabulary order:
-// B[j] = exp(x_j - m1), BX[j] = x_j, BI[j] = index, m1 = max x (sampling.rs:665-729).
-__device__ RowOut finish_list(float* B, float* BX, uint16_t* BI, int ns, float m1,
-                              const q3s_row_params& P, unsigned long long* keys, uint32_t* hist,
-                              float u, int n, const DebugRow& dbg) {
+// General path: mask, temperature, top-k, top-p and the draw over the full row
+// held as f32 in A (global workspace).  Kept out of line with scalar and
+// pointer arguments only, so the fast path's state stays in registers.
+__device__ __noinline__ unsigned long long general_compute(
+    float* A, float* GB, float* GBX, uint16_t* GBI, const uint32_t* bm, uint32_t* hist,
+    unsigned long long* keys, int n, float inv, float pf, int use_pen, int sf, int allow,
+    unsigned top_k, double top_p, float u, unsigned char* masks, float* probs) {
   const unsigned lane = lane_id();
-  float m2 = m1;
-  if (P.top_p < 1.0) {
-    const int st = apply_top_p(B, BX, BI, &ns, m1, P.top_p, keys, hist, &m2);
-    if (st != Q3S_STATUS_OK) return {st, 0u};
+  RowCtx rc;
+  rc.n = n;
+  rc.mis = 0;
+  rc.Q = 0;
+  rc.inv = inv;
+  rc.pf = pf;
+  rc.use_pen = use_pen != 0;
+  rc.sf = sf;
+  rc.allow = allow;
+  rc.bm = bm;
+  RowOut out{Q3S_STATUS_OK, 0u};
+  // Mask and temperature (sampling.rs:608-631).
+  float mx = neg_inf();
+  int nfin = 0;
+  bool nan_seen = false;
+  for (int i = lane; i < n; i += 32) {
+    const float x = xform<true, false>(A[i], i, rc);
+    A[i] = x;
+    mx = fmaxf(mx, x);
+    nfin += is_finite(x) ? 1 : 0;
+    nan_seen |= (x != x);
+    if (masks && is_finite(x)) masks[i] = 1;
   }
-
-  // Final softmax sum and the draw (sampling.rs:700-729).
-  const float sum = chain_sum(B, ns, true);
-  if (!is_finite(sum) || sum <= 0.0f) return {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
-  const float thr = __fmul_rn(u, sum);
-  int first = ns;
-  for (int j = lane; j < ns; j += 32) {
-    if (B[j] >= thr) {
-      first = j;
-      break;
+  mx = warp_max(mx);
+  nfin = __reduce_add_sync(FULL, nfin);
+  nan_seen = __any_sync(FULL, nan_seen);
+  __syncwarp();
+  if (nfin == 0) {
+    out = {sf >= 0 ? Q3S_STATUS_SUPPRESSION_NO_CANDIDATE : Q3S_STATUS_NO_CANDIDATE, 0u};
+  } else if (nan_seen || mx == __int_as_float(0x7f800000)) {
+    // A NaN or +inf after the temperature survives top-k and top-p and makes
+    // the softmax denominator non-finite (sampling.rs:675-678, 715-718).
+    out = {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
+  } else {
+    // Top-k threshold: the k-th largest finite value (sampling.rs:654-663).
+    float t = neg_inf();
+    if (top_k > 0u && (uint32_t)nfin > top_k) {
+      const uint32_t key = warp_select<uint32_t>(
+          n, top_k,
+          [&](int i, uint32_t& k) {
+            const float x = A[i];
+            k = ~total_key(x);
+            return x > neg_inf();
+          },
+          hist, 24);
+      t = from_total_key(~key);
     }
-  }
+    // Survivor list in vocabulary order.
+    int ns = 0;
+    for (int i0 = 0; i0 < n; i0 += 32) {
+      const int i = i0 + lane;
+      const float x = i < n ? A[i] : neg_inf();
+      const bool p = x >= t && x > neg_inf();
+      const unsigned b = __ballot_sync(FULL, p);
+      if (p) {
+        const int j = ns + __popc(b & lanemask_lt());
+        GBI[j] = (uint16_t)i;
+        GBX[j] = x;
+        GB[j] = cr_expf(__fsub_rn(x, mx));
+        if (masks) masks[i] |= 2;
+      }
+      ns += __popc(b);
+    }
+    __syncwarp();
+    float m2 = mx;
+    if (top_p < 1.0) {
+      const unsigned long long r = apply_top_p(GB, GBX, GBI, ns, mx, top_p, keys, hist);
+      const int st = (int)(r >> 56);
+      if (st != Q3S_STATUS_OK) {
+        out = {st, 0u};
+        ns = -1;
+      } else {
+        ns = (int)((r >> 32) & 0xFFFFFFu);
+        m2 = __uint_as_float((uint32_t)r);
+      }
+    }
+    if (ns >= 0) {
+      // Final softmax sum and the draw (sampling.rs:700-729).
+      const float sum = chain_sum(GB, ns, true);
+      if (!is_finite(sum) || sum <= 0.0f) {
+        out = {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
+      } else {
+        const float thr = __fmul_rn(u, sum);
+        int first = ns;
+        for (int j = lane; j < ns; j += 32) {
+          if (GB[j] >= thr) {
+            first = j;
+            break;
+          }
+        }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) first = min(first, __shfl_xor_sync(FULL, first, o));
-  const uint32_t token = first < ns ? (uint32_t)BI[first] : (uint32_t)(n - 1);
-  if (dbg.masks || dbg.probs) {
-    for (int j = lane; j < ns; j += 32) {
-      const int i = BI[j];
-      if (dbg.masks) dbg.masks[i] |= 4;
-      if (dbg.probs) {
-        const float e = cr_expf(__fsub_rn(BX[j], m2));
-        dbg.probs[i] = __double2float_rn((double)e / (double)sum);
+        for (int o = 16; o > 0; o >>= 1) first = min(first, __shfl_xor_sync(FULL, first, o));
+        out = {Q3S_STATUS_OK, first < ns ? (uint32_t)GBI[first] : (uint32_t)(n - 1)};
+        if (masks || probs) {
+          for (int j = lane; j < ns; j += 32) {
+            const int i = GBI[j];
+            if (masks) masks[i] |= 4;
+            if (probs) {
+              const float e = cr_expf(__fsub_rn(GBX[j], m2));
+              probs[i] = __double2float_rn((double)e / (double)sum);
+            }
+          }
+        }
       }
     }
   }
   __syncwarp();
-  return {Q3S_STATUS_OK, token};
+  return ((unsigned long long)(unsigned)out.status << 32) | out.token;
 }
 
-// ---------------------------------------------------------------------------
-// Row handlers.  Each releases the stage (`release`) exactly once, as soon as
-// it no longer reads it.
-// ---------------------------------------------------------------------------
+// ===========================================================================
+// Fast path: warp scan and candidate collection.
+// ===========================================================================
+
+// The stage is released (to the next row's copy) exactly once per row.
 struct Releaser {
   const KernelArgs* a;
   const FastSpace* f;
@@ -627,97 +714,6 @@ __device__ __forceinline__ void release(Releaser& r) {
     fence_proxy_async_smem();
     if (r.next < r.a->num_rows) issue_row<DT>(*r.a, r.next, *r.f);
   }
-}
-
-// Greedy row (sampling.rs:574-591) straight from the stage.
-template <int DT>
-__device__ RowOut greedy_stage(const FastSpace& f, const StageView& s, int sf, int allow) {
-  constexpr int EPV = Elem<DT>::EPV;
-  const unsigned lane = lane_id();
-  unsigned long long best = 0ull;
-  for (int q = lane; q < s.Q; q += 32) {
-    float e[EPV];
-    unpack<DT>(f.stage, q, e);
-#pragma unroll
-    for (int c = 0; c < EPV; ++c) {
-      const int i = q * EPV + c - s.mis;
-      if ((unsigned)i < (unsigned)s.n && is_finite(e[c]) && idx_allowed(i, sf, allow)) {
-        const unsigned long long k =
-            ((unsigned long long)total_key(e[c]) << 32) | (0xFFFFFFFFu - (uint32_t)i);
-        best = k > best ? k : best;
-      }
-    }
-  }
-  best = warp_max_u64(best);
-  if (best == 0ull) return {Q3S_STATUS_NO_CANDIDATE, 0u};
-  return {Q3S_STATUS_OK, 0xFFFFFFFFu - (uint32_t)best};
-}
-
-// General path: the full row as f32 in the global workspace, then full-row
-// passes (any top_k, any temperature).
-template <int DT>
-__device__ __noinline__ RowOut general_row(const FastSpace& f, const GenSpace& g, const StageView& s,
-                              const q3s_row_params& P, const RowCtx& rc, float u, Releaser& rel,
-                              const DebugRow& dbg) {
-  const unsigned lane = lane_id();
-  const int n = s.n;
-  float* A = g.A;
-  for (int i = lane; i < n; i += 32) A[i] = stage_elem<DT>(f.stage, s.mis, i);
-  __syncwarp();
-  release<DT>(rel);
-  // Mask and temperature (sampling.rs:608-631).
-  float mx = neg_inf();
-  int nfin = 0;
-  bool nan_seen = false;
-  for (int i = lane; i < n; i += 32) {
-    const float x = xform<true, false>(A[i], i, rc);
-    A[i] = x;
-    mx = fmaxf(mx, x);
-    nfin += is_finite(x) ? 1 : 0;
-    nan_seen |= (x != x);
-    if (dbg.masks && is_finite(x)) dbg.masks[i] = 1;
-  }
-  mx = warp_max(mx);
-  nfin = __reduce_add_sync(FULL, nfin);
-  nan_seen = __any_sync(FULL, nan_seen);
-  __syncwarp();
-  if (nfin == 0)
-    return {rc.sf >= 0 ? Q3S_STATUS_SUPPRESSION_NO_CANDIDATE : Q3S_STATUS_NO_CANDIDATE, 0u};
-  // A NaN or +inf after the temperature survives top-k and top-p and makes
-  // the softmax denominator non-finite (sampling.rs:675-678, 715-718).
-  if (nan_seen || mx == __int_as_float(0x7f800000)) return {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
-  // Top-k threshold: the k-th largest finite value (sampling.rs:654-663).
-  float t = neg_inf();
-  if (P.top_k > 0u && (uint32_t)nfin > P.top_k) {
-    const uint32_t key = warp_select<uint32_t>(
-        n, P.top_k,
-        [&](int i, uint32_t& k) {
-          const float x = A[i];
-          k = ~total_key(x);
-          return x > neg_inf();
-        },
-        f.hist, 24);
-    t = from_total_key(~key);
-  }
-  // Survivor list in vocabulary order.
-  int ns = 0;
-  for (int i0 = 0; i0 < n; i0 += 32) {
-    const int i = i0 + lane;
-    const float x = i < n ? A[i] : neg_inf();
-    const bool p = x >= t && x > neg_inf();
-    const unsigned b = __ballot_sync(FULL, p);
-    if (p) {
-      const int j = ns + __popc(b & lanemask_lt());
-      g.BI[j] = (uint16_t)i;
-      g.BX[j] = x;
-      g.B[j] = cr_expf(__fsub_rn(x, mx));
-      if (dbg.masks) dbg.masks[i] |= 2;
-    }
-    ns += __popc(b);
-  }
-  __syncwarp();
-  return finish_list(g.B, g.BX, g.BI, ns, mx, P, reinterpret_cast<unsigned long long*>(f.cand),
-                     f.hist, u, n, dbg);
 }
 
 // Vector maxima of the stage (registers) and the row maximum.
@@ -750,17 +746,66 @@ __device__ __forceinline__ int count_ge(const float (&vm)[NJ], float tau) {
   return (int)__reduce_add_sync(FULL, (unsigned)c);
 }
 
-// Candidates {x >= tau} of the flagged vectors, each lane into its own slots
-// of f.cand (slot t of lane l at t*32 + l: conflict-free), as (x after the
-// temperature, index).  Returns this lane's count (above SEG: overflow).
-template <int DT, int NJ, bool XF, bool EDGE>
-__device__ int collect(const FastSpace& f, const RowCtx& r, const float (&vm)[NJ], float tau) {
+// A distance d below the row maximum such that between k and hi vectors have
+// their maximum at or above mx - d.  Starts from the warp's previous distance;
+// false when no finite threshold reaches k vectors.
+template <int NJ>
+__device__ bool find_tau(const float (&vm)[NJ], float mx, int k, int hi, float& delta,
+                         float& tau) {
+  float lo = 0.0f, dhi = -1.0f, best = -1.0f;
+  float d = delta > 0.0f ? delta : 1.0f;
+#pragma unroll 1
+  for (int it = 0; it < 48; ++it) {
+    const float t = __fsub_rn(mx, d);
+    if (!(t > neg_inf())) break;
+    const int c = count_ge(vm, t);
+    if (c >= k) best = best < 0.0f ? d : fminf(best, d);
+    if (c < k) {
+      lo = d;
+      d = dhi < 0.0f ? __fmul_rn(d, 4.0f) : 0.5f * (lo + dhi);
+    } else if (c > hi) {
+      dhi = d;
+      d = 0.5f * (lo + dhi);
+    } else {
+      delta = d;
+      tau = t;
+      return true;
+    }
+    if (dhi >= 0.0f && !(dhi - lo > 0.0f)) break;
+    if (!(d < __int_as_float(0x7f800000))) break;
+  }
+  if (best < 0.0f) return false;
+  delta = best;
+  tau = __fsub_rn(mx, best);
+  return tau > neg_inf();
+}
+
+// Number of this lane's candidates {x >= tau} in its flagged vectors.
+template <int DT, bool XF, bool EDGE>
+__device__ __forceinline__ int count_cands(const FastSpace& f, const RowCtx& r, uint64_t flags,
+                                           float tau) {
   constexpr int EPV = Elem<DT>::EPV;
   const int lane = (int)lane_id();
-  uint64_t flags = 0;
-#pragma unroll
-  for (int j = 0; j < NJ; ++j) flags |= (vm[j] >= tau ? 1ull : 0ull) << j;
   int cnt = 0;
+  while (flags) {
+    const int j = __ffsll((long long)flags) - 1;
+    flags &= flags - 1;
+    const int q = lane + 32 * j;
+    float e[EPV];
+    unpack<DT>(f.stage, q, e);
+#pragma unroll
+    for (int c = 0; c < EPV; ++c) cnt += xform<XF, EDGE>(e[c], q * EPV + c - r.mis, r) >= tau ? 1 : 0;
+  }
+  return cnt;
+}
+
+// Writes this lane's candidates as (x after the temperature, index).
+template <int DT, bool XF, bool EDGE>
+__device__ __forceinline__ void write_cands(const FastSpace& f, const RowCtx& r, uint64_t flags,
+                                            float tau, uint2* dst) {
+  constexpr int EPV = Elem<DT>::EPV;
+  const int lane = (int)lane_id();
+  int t = 0;
   while (flags) {
     const int j = __ffsll((long long)flags) - 1;
     flags &= flags - 1;
@@ -771,118 +816,191 @@ __device__ int collect(const FastSpace& f, const RowCtx& r, const float (&vm)[NJ
     for (int c = 0; c < EPV; ++c) {
       const float x = xform<XF, EDGE>(e[c], q * EPV + c - r.mis, r);
       if (x >= tau) {
-        if (cnt < SEG) {
-          const float xv = XF ? x : __fmul_rn(x, r.inv);
-          f.cand[cnt * 32 + lane] = make_uint2(__float_as_uint(xv), (uint32_t)(q * EPV + c - r.mis));
-        }
-        ++cnt;
+        const float xv = XF ? x : __fmul_rn(x, r.inv);
+        dst[t++] = make_uint2(__float_as_uint(xv), (uint32_t)(q * EPV + c - r.mis));
       }
     }
+  }
+}
+
+// ===========================================================================
+// Fast path: one lane finishes one row from its candidate list.
+// ===========================================================================
+
+__device__ __forceinline__ float ex(const uint2& e) { return __uint_as_float(e.x); }
+__device__ __forceinline__ uint32_t kx(const uint2& e) { return total_key(__uint_as_float(e.x)); }
+
+// Shell sort gaps (Ciura's sequence).
+__constant__ int kGaps[7] = {301, 132, 57, 23, 10, 4, 1};
+
+// Shell sort of E[0..s) by index ascending, moving P along when given.
+__device__ __forceinline__ void sort_by_index(uint2* E, float* P, int s) {
+#pragma unroll 1
+  for (int gi = 0; gi < 7; ++gi) {
+    const int g = kGaps[gi];
+#pragma unroll 1
+    for (int i = g; i < s; ++i) {
+      const uint2 v = E[i];
+      const float pv = P ? P[i] : 0.0f;
+      int j = i;
+      while (j >= g && E[j - g].y > v.y) {
+        E[j] = E[j - g];
+        if (P) P[j] = P[j - g];
+        j -= g;
+      }
+      E[j] = v;
+      if (P) P[j] = pv;
+    }
+  }
+}
+
+// Shell sort of (E, P) by (p desc, index asc).
+__device__ __forceinline__ void sort_by_prob(uint2* E, float* P, int s) {
+#pragma unroll 1
+  for (int gi = 0; gi < 7; ++gi) {
+    const int g = kGaps[gi];
+#pragma unroll 1
+    for (int i = g; i < s; ++i) {
+      const uint2 v = E[i];
+      const float pv = P[i];
+      int j = i;
+      while (j >= g && (P[j - g] < pv || (P[j - g] == pv && E[j - g].y > v.y))) {
+        E[j] = E[j - g];
+        P[j] = P[j - g];
+        j -= g;
+      }
+      E[j] = v;
+      P[j] = pv;
+    }
+  }
+}
+
+// Finishes one row from its candidates E[0..c) (x bits, index), c >= k:
+// the statements of sampling.rs:654-729 restricted to the candidate set,
+// which holds every value >= the k-th largest.  P: scratch of c floats when
+// use_top_p.  Writes the top-k threshold to *t_out.
+__device__ RowOut lane_finish(uint2* E, float* P, int c, int k, int n, float Mx, float u,
+                              bool use_top_p, float top_p, float* t_out, unsigned char* masks,
+                              float* probs) {
+  // k-th largest x: quickselect (Hoare partition, descending keys).
+  int lo = 0, hi = c - 1;
+  const int target = k - 1;
+  uint32_t tkey;
+#pragma unroll 1
+  for (;;) {
+    if (lo >= hi) {
+      tkey = kx(E[target]);
+      break;
+    }
+    const uint32_t a = kx(E[lo]), b = kx(E[(lo + hi) >> 1]), d = kx(E[hi]);
+    const uint32_t pv = max(min(a, b), min(max(a, b), d));  // median of three
+    int i = lo, j = hi;
+    while (i <= j) {
+      while (i <= hi && kx(E[i]) > pv) ++i;
+      while (j >= lo && kx(E[j]) < pv) --j;
+      if (i <= j) {
+        const uint2 tmp = E[i];
+        E[i] = E[j];
+        E[j] = tmp;
+        ++i;
+        --j;
+      }
+    }
+    if (target <= j) {
+      hi = j;
+    } else if (target >= i) {
+      lo = i;
+    } else {
+      tkey = pv;
+      break;
+    }
+  }
+  const float t = from_total_key(tkey);
+  *t_out = t;
+  // Survivors x >= t (sampling.rs:657-662), then vocabulary order.
+  int s = 0;
+  for (int j = 0; j < c; ++j)
+    if (ex(E[j]) >= t) E[s++] = E[j];
+  sort_by_index(E, nullptr, s);
+  float m2 = Mx;
+  int ns = s;
+  if (use_top_p) {
+    // Denominator in vocabulary order (sampling.rs:666-679).
+    float total = 0.0f;
+    for (int j = 0; j < s; ++j) {
+      const float e = cr_expf(__fsub_rn(ex(E[j]), Mx));
+      P[j] = e;
+      total = __fadd_rn(total, e);
+    }
+    if (!is_finite(total) || total <= 0.0f) return {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
+    const float inv_total = __fdiv_rn(1.0f, total);
+    const float cutoff = __fsub_rn(Mx, 16.0f);
+    for (int j = 0; j < s; ++j) P[j] = ex(E[j]) >= cutoff ? __fmul_rn(P[j], inv_total) : 0.0f;
+    // Nucleus in (p desc, index asc) order (sampling.rs:690-697).
+    sort_by_prob(E, P, s);
+    float cum = 0.0f;
+    int keep = 0;
+    for (int j = 0; j < s && P[j] > 0.0f; ++j) {
+      if (j > 0 && cum >= top_p) break;
+      cum = __fadd_rn(cum, P[j]);
+      keep = j + 1;
+    }
+    ns = keep;
+    sort_by_index(E, nullptr, ns);
+    m2 = neg_inf();
+    for (int j = 0; j < ns; ++j) m2 = fmaxf(m2, ex(E[j]));
+    if (!(m2 > neg_inf())) return {Q3S_STATUS_NO_CANDIDATE, 0u};
+  }
+  // Final softmax and the vocabulary-order draw (sampling.rs:700-729).
+  float sum = 0.0f;
+  for (int j = 0; j < ns; ++j) {
+    const float e = cr_expf(__fsub_rn(ex(E[j]), m2));
+    E[j].x = __float_as_uint(e);
+    sum = __fadd_rn(sum, e);
+  }
+  if (!is_finite(sum) || sum <= 0.0f) return {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
+  const float thr = __fmul_rn(u, sum);
+  float cum = 0.0f;
+  uint32_t token = (uint32_t)(n - 1);
+  for (int j = 0; j < ns; ++j) {
+    cum = __fadd_rn(cum, ex(E[j]));
+    if (cum >= thr) {
+      token = E[j].y;
+      break;
+    }
+  }
+  if (masks || probs) {
+    for (int j = 0; j < ns; ++j) {
+      if (masks) masks[E[j].y] |= 4;
+      if (probs) probs[E[j].y] = __double2float_rn((double)ex(E[j]) / (double)sum);
+    }
+  }
+  return {Q3S_STATUS_OK, token};
+}
+
+// Every lane finishes the pending row of its slot.
+__device__ __forceinline__ void flush_slots(const KernelArgs& a, const FastSpace& f, int nslots) {
+  __syncwarp();
+  const int b = (int)lane_id();
+  if (b < nslots) {
+    const Slot sl = f.slots[b];
+    uint2* E = f.arena + sl.off;
+    float t;
+    const RowOut o = lane_finish(E, reinterpret_cast<float*>(E + sl.c), sl.c, sl.k, sl.n, sl.Mx,
+                                 sl.u, sl.use_top_p != 0, sl.top_p, &t, nullptr, nullptr);
+    a.tokens[sl.row] = o.token;
+    a.status[sl.row] = (unsigned char)o.status;
   }
   __syncwarp();
-  return cnt;
 }
 
-// Exact k-th largest x among the candidates (each lane holds `mine` of
-// them).  Bins of equal width over the current value range, counted from the
-// top; the range narrows to the bin that holds the k-th value until that bin
-// holds one value (or one distinct value).  The bin function
-// floor((x - lo) * scale) is monotone in x, so the bins partition the
-// candidates in value order.
-__device__ float select_kth_candidate(const FastSpace& f, int mine, int k) {
-  const unsigned lane = lane_id();
-  float lo = __int_as_float(0x7f800000), hi = neg_inf();
-  for (int t = 0; t < mine; ++t) {
-    const float x = __uint_as_float(f.cand[t * 32 + lane].x);
-    lo = fminf(lo, x);
-    hi = fmaxf(hi, x);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    lo = fminf(lo, __shfl_xor_sync(FULL, lo, o));
-    hi = fmaxf(hi, __shfl_xor_sync(FULL, hi, o));
-  }
-  uint32_t kk = (uint32_t)k;
-#pragma unroll 1
-  for (int pass = 0; pass < 8; ++pass) {
-    if (!(hi > lo)) return hi;  // one distinct value left
-    const float width = __fsub_rn(hi, lo);
-    if (!(width < __int_as_float(0x7f800000))) break;  // range too wide: key radix below
-    const float scale = __fdiv_rn(63.5f, width);
-    // 64 bins, counted in f.hist.
-    f.hist[lane] = 0u;
-    f.hist[lane + 32] = 0u;
-    __syncwarp();
-    for (int t = 0; t < mine; ++t) {
-      const float x = __uint_as_float(f.cand[t * 32 + lane].x);
-      if (x >= lo && x <= hi) {
-        const int b = min(63, (int)__fmul_rn(__fsub_rn(x, lo), scale));
-        atomicAdd(&f.hist[b], 1u);
-      }
-    }
-    __syncwarp();
-    // Lane l owns bins 63-2l and 62-2l (counted from the top).
-    const uint32_t c0 = f.hist[63 - 2 * lane], c1 = f.hist[62 - 2 * lane];
-    const uint32_t s = c0 + c1;
-    const uint32_t incl = warp_inclusive_scan(s);
-    const unsigned ball = __ballot_sync(FULL, incl >= kk);
-    const int src = ball ? __ffs(ball) - 1 : 31;
-    int bin = 0;
-    uint32_t before = 0, inbin = 0;
-    if ((int)lane == src) {
-      const uint32_t acc = incl - s;
-      if (acc + c0 >= kk) {
-        bin = 63 - 2 * lane;
-        before = acc;
-        inbin = c0;
-      } else {
-        bin = 62 - 2 * lane;
-        before = acc + c0;
-        inbin = c1;
-      }
-    }
-    bin = __shfl_sync(FULL, bin, src);
-    before = __shfl_sync(FULL, before, src);
-    inbin = __shfl_sync(FULL, inbin, src);
-    kk -= before;
-    // Value range of the chosen bin.
-    float nlo = __int_as_float(0x7f800000), nhi = neg_inf();
-    for (int t = 0; t < mine; ++t) {
-      const float x = __uint_as_float(f.cand[t * 32 + lane].x);
-      if (x >= lo && x <= hi && min(63, (int)__fmul_rn(__fsub_rn(x, lo), scale)) == bin) {
-        nlo = fminf(nlo, x);
-        nhi = fmaxf(nhi, x);
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      nlo = fminf(nlo, __shfl_xor_sync(FULL, nlo, o));
-      nhi = fmaxf(nhi, __shfl_xor_sync(FULL, nhi, o));
-    }
-    lo = nlo;
-    hi = nhi;
-    if (inbin == 1u) return hi;
-    __syncwarp();
-  }
-  // Fallback: radix selection on total-order keys below the current range.
-  const uint32_t kmax = total_key(hi);
-  const uint32_t kspan = kmax - total_key(lo);
-  const int bits = 32 - __clz(kspan | 1u);
-  const int top = ((bits + 7) / 8) * 8 - 8;
-  const float flo = lo, fhi = hi;
-  // warp_select visits slot j = t*32 + lane from lane `lane`: its own slots.
-  const uint32_t rel_k = warp_select<uint32_t>(
-      32 * SEG, kk,
-      [&](int j, uint32_t& key) {
-        const float x = __uint_as_float(f.cand[j].x);
-        key = kmax - total_key(x);
-        return (j >> 5) < mine && x >= flo && x <= fhi;
-      },
-      f.hist, top);
-  return from_total_key(kmax - rel_k);
-}
+// Pending-row bookkeeping of a warp.
+struct Batch {
+  int nslots;
+  int used;  // arena entries in use
+};
 
-// Debug pass over the stage: bit0 finite x, bit1 x >= t.
+// Debug pass over the stage: bit0 finite x, bit1 x >= t (OR-ed in).
 template <int DT, bool XF>
 __device__ void debug_masks(const FastSpace& f, const RowCtx& r, float t, unsigned char* masks) {
   const unsigned lane = lane_id();
@@ -892,73 +1010,43 @@ __device__ void debug_masks(const FastSpace& f, const RowCtx& r, float t, unsign
     unsigned char m = 0;
     if (is_finite(x)) m = 1;
     if (is_finite(x) && x >= t) m |= 2;
-    masks[i] = m;
+    masks[i] |= m;
   }
   __syncwarp();
 }
 
-// Fast path; returns false (before releasing the stage) when the row must
-// take the general path instead.
+enum { FAST_PENDING = 0, FAST_DONE = 1, FAST_GENERAL = 2 };
+
+// Scans the staged row and appends its candidates as a pending slot.
+// FAST_PENDING: slot recorded, stage released.  FAST_DONE: `out` holds the
+// result, stage released.  FAST_GENERAL: the row needs the general path; the
+// stage is still held.
 template <int DT, int NJ, bool XF, bool EDGE>
-__device__ bool fast_row(const FastSpace& f, const StageView& s, const q3s_row_params& P,
-                         const RowCtx& rc, float u, Releaser& rel, const DebugRow& dbg,
-                         float& delta, RowOut& out) {
-  const unsigned lane = lane_id();
-  const int n = s.n;
+__device__ int fast_row(const KernelArgs& a, const FastSpace& f, const StageView& s,
+                        const RowMeta& m, const RowCtx& rc, float u, long long row, Releaser& rel,
+                        float& delta, Batch& batch, RowOut& out, const DebugRow& dbg) {
+  const q3s_row_params& P = m.P;
   float vm[NJ];
   const float mx = scan_stage<DT, NJ, XF, EDGE>(f, rc, vm);
-  // Row maximum in the x domain.
-  if (!XF && mx == __int_as_float(0x7f800000)) return false;  // raw +inf: general path
+  if (!XF && mx == __int_as_float(0x7f800000)) return FAST_GENERAL;  // raw +inf
   if (mx == neg_inf() || mx != mx) {
     release<DT>(rel);
     out = {rc.sf >= 0 ? Q3S_STATUS_SUPPRESSION_NO_CANDIDATE : Q3S_STATUS_NO_CANDIDATE, 0u};
-    return true;
+    return FAST_DONE;
   }
   const float Mx = XF ? mx : __fmul_rn(mx, rc.inv);
   if (Mx == __int_as_float(0x7f800000)) {
     release<DT>(rel);
     out = {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
-    return true;
+    return FAST_DONE;
   }
-  // Threshold on the vector maxima: count in [k, hi].
   const int k = (int)P.top_k;
   const int hi = k <= 128 ? max(2 * k, 64) : k + 96;
-  float vmin = __int_as_float(0x7f800000);
-#pragma unroll
-  for (int j = 0; j < NJ; ++j)
-    if (vm[j] > neg_inf()) vmin = fminf(vmin, vm[j]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) vmin = fminf(vmin, __shfl_xor_sync(FULL, vmin, o));
-  const float span = __fsub_rn(mx, vmin);
-  if (!(span < __int_as_float(0x7f800000))) return false;
-  if (count_ge(vm, vmin) < k) return false;  // fewer than k finite vectors
-  float lo = 0.0f, hiD = span;
-  bool hi_known = false;
-  float d = (delta > 0.0f && delta <= span) ? delta : span * 0.25f;
-  float best = span;  // smallest distance seen whose count reaches k
-  bool accepted = false;
-#pragma unroll 1
-  for (int it = 0; it < 24; ++it) {
-    const int c = count_ge(vm, __fsub_rn(mx, d));
-    if (c >= k) best = fminf(best, d);
-    if (c < k) {
-      lo = d;
-      d = hi_known ? 0.5f * (lo + hiD) : fminf(span, d > 0.0f ? 2.0f * d : span * 0.0625f);
-    } else if (c > hi) {
-      hiD = d;
-      hi_known = true;
-      d = 0.5f * (lo + hiD);
-    } else {
-      accepted = true;
-      break;
-    }
-    if (hiD - lo <= 0.0f) break;
-  }
-  if (!accepted) d = best;
-  float tau = __fsub_rn(mx, d);
+  float tau;
+  if (!find_tau(vm, mx, k, hi, delta, tau)) return FAST_GENERAL;
   // Raw-domain selection: lower tau until its image lies strictly below the
-  // image of every value that reaches the chosen count, so no element with
-  // v < tau can tie the k-th largest x after the multiply.
+  // image of tau, so no element below the new tau can tie the k-th largest
+  // x after the multiply.
   if (!XF && rc.inv != 1.0f) {
     const float img = __fmul_rn(tau, rc.inv);
     float t2 = tau;
@@ -968,65 +1056,96 @@ __device__ bool fast_row(const FastSpace& f, const StageView& s, const q3s_row_p
       t2 = __fsub_rn(t2, fmaxf(fabsf(t2) * 3.814697265625e-06f, 1.1754944e-38f));
       ok = __fmul_rn(t2, rc.inv) < img;
     }
-    if (!ok) return false;
+    if (!ok) return FAST_GENERAL;
     tau = t2;
   }
-  const int mine = collect<DT, NJ, XF, EDGE>(f, rc, vm, tau);
-  const bool overflow = __any_sync(FULL, mine > SEG);
-  const int c = (int)__reduce_add_sync(FULL, (unsigned)mine);
-  // The survivors (at most c) must fit the list; decided before release.
-  if (overflow || c < k || c > LCAP) return false;
-  delta = d;
-  if (!dbg.masks) release<DT>(rel);
-
-  // Exact k-th largest candidate.
-  const float t = select_kth_candidate(f, mine, k);
-  // The debug masks recompute x with the history bitmap, which the survivor
-  // bitmap below overwrites.
-  if (dbg.masks) debug_masks<DT, XF>(f, rc, t, dbg.masks);
-  // Survivors x >= t, in vocabulary order through a bitmap.
-  const int words = (n + 31) >> 5;
-  for (int w = lane; w < words; w += 32) f.bm[w] = 0u;
-  __syncwarp();
-  for (int s = 0; s < mine; ++s) {
-    const uint2 e = f.cand[s * 32 + lane];
-    if (__uint_as_float(e.x) >= t) atomicOr(&f.bm[e.y >> 5], 1u << (e.y & 31));
+  uint64_t flags = 0;
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) flags |= (vm[j] >= tau ? 1ull : 0ull) << j;
+  const int mine = count_cands<DT, XF, EDGE>(f, rc, flags, tau);
+  const int incl = (int)warp_inclusive_scan((uint32_t)mine);
+  const int c = __shfl_sync(FULL, incl, 31);
+  if (c < k || c > ROW_CAP) return FAST_GENERAL;
+  const bool use_top_p = P.top_p < 1.0;
+  const int need = c + (use_top_p ? (c + 1) / 2 : 0);
+  if (batch.used + need > ARENA || dbg.masks) {
+    flush_slots(a, f, batch.nslots);
+    batch.nslots = 0;
+    batch.used = 0;
   }
+  uint2* base = f.arena + batch.used;
+  write_cands<DT, XF, EDGE>(f, rc, flags, tau, base + (incl - mine));
   __syncwarp();
-  const int per = (words + 31) >> 5;
-  const int w0 = min(words, (int)lane * per), w1 = min(words, w0 + per);
-  int own = 0;
-  for (int w = w0; w < w1; ++w) own += __popc(f.bm[w]);
-  const int incl = (int)warp_inclusive_scan((uint32_t)own);
-  int run = incl - own;
-  for (int w = w0; w < w1; ++w) {
-    f.wpre[w] = (uint16_t)run;
-    run += __popc(f.bm[w]);
+  if (dbg.masks) {
+    // Debug rows finish at once (lane 0) while the stage is still held.
+    float t = 0.0f;
+    RowOut o{0, 0u};
+    if (lane_id() == 0)
+      o = lane_finish(base, reinterpret_cast<float*>(base + c), c, k, s.n, Mx, u, use_top_p,
+                      (float)P.top_p, &t, dbg.masks, dbg.probs);
+    __syncwarp();
+    t = __shfl_sync(FULL, t, 0);
+    o.status = __shfl_sync(FULL, o.status, 0);
+    o.token = __shfl_sync(FULL, o.token, 0);
+    debug_masks<DT, XF>(f, rc, t, dbg.masks);
+    release<DT>(rel);
+    out = o;
+    return FAST_DONE;
   }
-  const int ns = __shfl_sync(FULL, incl, 31);
-  __syncwarp();
-  for (int s = 0; s < mine; ++s) {
-    const uint2 e = f.cand[s * 32 + lane];
-    const float x = __uint_as_float(e.x);
-    if (x >= t) {
-      const uint32_t w = e.y >> 5, b = e.y & 31;
-      const int p = f.wpre[w] + __popc(f.bm[w] & ((1u << b) - 1u));
-      f.BI[p] = (uint16_t)e.y;
-      f.BX[p] = x;
-      f.B[p] = cr_expf(__fsub_rn(x, Mx));
-    }
-  }
-  __syncwarp();
-  out = finish_list(f.B, f.BX, f.BI, ns, Mx, P, reinterpret_cast<unsigned long long*>(f.cand),
-                    f.hist, u, n, dbg);
   release<DT>(rel);
-  return true;
+  if (lane_id() == 0) {
+    Slot& sl = f.slots[batch.nslots];
+    sl.row = row;
+    sl.off = batch.used;
+    sl.c = c;
+    sl.k = k;
+    sl.n = s.n;
+    sl.Mx = Mx;
+    sl.u = u;
+    sl.top_p = (float)P.top_p;
+    sl.use_top_p = use_top_p ? 1 : 0;
+  }
+  batch.nslots += 1;
+  batch.used += need;
+  if (batch.nslots == MAX_SLOTS) {
+    flush_slots(a, f, batch.nslots);
+    batch.nslots = 0;
+    batch.used = 0;
+  }
+  return FAST_PENDING;
 }
 
+// Greedy row (sampling.rs:574-591) straight from the stage.
+template <int DT>
+__device__ RowOut greedy_stage(const FastSpace& f, const StageView& s, int sf, int allow) {
+  constexpr int EPV = Elem<DT>::EPV;
+  const unsigned lane = lane_id();
+  unsigned long long best = 0ull;
+  for (int q = lane; q < s.Q; q += 32) {
+    float e[EPV];
+    unpack<DT>(f.stage, q, e);
+#pragma unroll
+    for (int c = 0; c < EPV; ++c) {
+      const int i = q * EPV + c - s.mis;
+      if ((unsigned)i < (unsigned)s.n && is_finite(e[c]) && idx_allowed(i, sf, allow)) {
+        const unsigned long long k =
+            ((unsigned long long)total_key(e[c]) << 32) | (0xFFFFFFFFu - (uint32_t)i);
+        best = k > best ? k : best;
+      }
+    }
+  }
+  best = warp_max_u64(best);
+  if (best == 0ull) return {Q3S_STATUS_NO_CANDIDATE, 0u};
+  return {Q3S_STATUS_OK, 0xFFFFFFFFu - (uint32_t)best};
+}
+
+// A sampled row: fast path when it applies, else the general path (after the
+// warp's pending rows are finished, since the general path borrows the arena).
+// Returns false when the row is pending in the batch.
 template <int DT, int NJ>
-__device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const GenSpace& g,
-                              const RowMeta& m, const StageView& s, Releaser& rel, float& delta,
-                              const DebugRow& dbg) {
+__device__ bool sampled_row(const KernelArgs& a, const FastSpace& f, const GenSpace& g,
+                            const RowMeta& m, const StageView& s, long long row, Releaser& rel,
+                            float& delta, Batch& batch, RowOut& out, const DebugRow& dbg) {
   const q3s_row_params& P = m.P;
   RowCtx rc;
   rc.n = s.n;
@@ -1045,17 +1164,29 @@ __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const Gen
   if (fast) {
     const bool xf = rc.use_pen || rc.sf >= 0;
     const bool edge = s.mis != 0 || (s.n % Elem<DT>::EPV) != 0;
-    RowOut out;
-    bool done;
+    int r;
     if (xf)
-      done = edge ? fast_row<DT, NJ, true, true>(f, s, P, rc, u, rel, dbg, delta, out)
-                  : fast_row<DT, NJ, true, false>(f, s, P, rc, u, rel, dbg, delta, out);
+      r = edge ? fast_row<DT, NJ, true, true>(a, f, s, m, rc, u, row, rel, delta, batch, out, dbg)
+               : fast_row<DT, NJ, true, false>(a, f, s, m, rc, u, row, rel, delta, batch, out, dbg);
     else
-      done = edge ? fast_row<DT, NJ, false, true>(f, s, P, rc, u, rel, dbg, delta, out)
-                  : fast_row<DT, NJ, false, false>(f, s, P, rc, u, rel, dbg, delta, out);
-    if (done) return out;
+      r = edge ? fast_row<DT, NJ, false, true>(a, f, s, m, rc, u, row, rel, delta, batch, out, dbg)
+               : fast_row<DT, NJ, false, false>(a, f, s, m, rc, u, row, rel, delta, batch, out, dbg);
+    if (r == FAST_PENDING) return false;
+    if (r == FAST_DONE) return true;
   }
-  return general_row<DT>(f, g, s, P, rc, u, rel, dbg);
+  flush_slots(a, f, batch.nslots);
+  batch.nslots = 0;
+  batch.used = 0;
+  const unsigned lane = lane_id();
+  for (int i = lane; i < s.n; i += 32) g.A[i] = stage_elem<DT>(f.stage, s.mis, i);
+  __syncwarp();
+  release<DT>(rel);
+  const unsigned long long r = general_compute(
+      g.A, g.B, g.BX, g.BI, f.bm, f.hist, reinterpret_cast<unsigned long long*>(f.arena), s.n,
+      rc.inv, rc.pf, rc.use_pen ? 1 : 0, rc.sf, rc.allow, P.top_k, P.top_p, u, dbg.masks,
+      dbg.probs);
+  out = {(int)(r >> 32), (uint32_t)r};
+  return true;
 }
 
 template <int DT, int NJ>
@@ -1079,6 +1210,7 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
   if (row < a.num_rows && lane == 0) issue_row<DT>(a, row, f);
   uint32_t phase = 0;
   float delta = 0.0f;
+  Batch batch{0, 0};
   // Per-row metadata is loaded one row ahead so its latency overlaps a row.
   RowMeta cur;
   if (row < a.num_rows) cur = load_meta(a, row);
@@ -1098,24 +1230,22 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
       for (int i = lane; i < n; i += 32) dbg.probs[i] = 0.0f;
     // History bitmap of a sampled row with a penalty (filled while the
     // stage copy is in flight).
-    if (st == Q3S_STATUS_OK && P.do_sample && P.repetition_penalty != 1.0) {
-      const long long h0 = cur.h0, h1 = cur.h1;
-      if (h1 > h0) {
-        const int words = (n + 31) >> 5;
-        for (int w = lane; w < words; w += 32) f.bm[w] = 0u;
-        __syncwarp();
-        for (long long h = h0 + lane; h < h1; h += 32) {
-          const int id = a.history[h];
-          if (id < n) atomicOr(&f.bm[id >> 5], 1u << (id & 31));
-        }
-        __syncwarp();
+    if (st == Q3S_STATUS_OK && P.do_sample && P.repetition_penalty != 1.0 && cur.h1 > cur.h0) {
+      const int words = (n + 31) >> 5;
+      for (int w = lane; w < words; w += 32) f.bm[w] = 0u;
+      __syncwarp();
+      for (long long h = cur.h0 + lane; h < cur.h1; h += 32) {
+        const int id = a.history[h];
+        if (id < n) atomicOr(&f.bm[id >> 5], 1u << (id & 31));
       }
+      __syncwarp();
     }
     const bool ready = mbar_wait_bounded(f.mbar, phase, WAIT_LIMIT_NS);
     phase ^= 1u;
     if (!ready) {
-      // The stage never arrived: mark this warp's remaining rows and stop
-      // after giving the copy in flight another bounded wait.
+      // The stage never arrived: finish what is pending, mark this warp's
+      // remaining rows and stop after another bounded wait for the copy.
+      flush_slots(a, f, batch.nslots);
       mbar_wait_bounded(f.mbar, phase ^ 1u, WAIT_LIMIT_NS);
       for (long long r = row; r < a.num_rows; r += stride)
         if (lane == 0) {
@@ -1125,23 +1255,24 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
       return;
     }
     RowOut out{st, 0u};
+    bool have = true;
     if (st == Q3S_STATUS_OK) {
       const StageView s = complete_stage<DT>(a, row, n, f);
       if (!P.do_sample) {
         out = greedy_stage<DT>(f, s, P.suppress_from, P.allow_token);
-        release<DT>(rel);
       } else {
-        out = sampled_row<DT, NJ>(a, f, g, cur, s, rel, delta, dbg);
+        have = sampled_row<DT, NJ>(a, f, g, cur, s, row, rel, delta, batch, out, dbg);
       }
     }
     release<DT>(rel);
-    if (lane == 0) {
+    if (have && lane == 0) {
       a.tokens[row] = out.token;
       a.status[row] = (unsigned char)out.status;
     }
     __syncwarp();
     cur = nxt;
   }
+  flush_slots(a, f, batch.nslots);
 }
 
 // Greedy argmax rows (sampling.rs:40-60 and :72-117), one warp per row.
