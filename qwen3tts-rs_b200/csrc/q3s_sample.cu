@@ -25,14 +25,14 @@
 //   2. it picks a threshold tau on the vector maxima such that at least k
 //      vectors (hence at least k elements) reach it, so the candidates
 //      {x >= tau} contain the whole top-k set, ties included;
-//   3. it re-reads only the vectors whose maximum reaches tau and appends
-//      their candidates (a few dozen to a few hundred per row) to a per-warp
-//      arena, then releases the stage to the next row's copy;
-//   4. once 32 rows are pending (or the arena is full), each lane finishes
-//      one row from its candidate list: exact k-th largest by quickselect,
-//      survivors sorted into vocabulary order, top-p and the draw.  The
-//      sequential sums are sequential per lane anyway, and 32 rows proceed
-//      in parallel without warp-level synchronisation.
+//   3. it re-reads only the vectors whose maximum reaches tau and gathers
+//      their candidates (a few dozen to a few hundred per row) into a short
+//      list, then releases the stage to the next row's copy;
+//   4. the list is finished warp-cooperatively with register bitonic sorts
+//      of 32-bit keys (32, 128 or 512 of them): one sort gives the exact
+//      k-th largest, a second puts the survivors in vocabulary order, top-p
+//      sorts by (p desc, index asc) and back; each sequential f32 chain runs
+//      on one lane over a shared-memory array in that order.
 // Rows outside the fast path (top_k off or above 256, a temperature whose
 // reciprocal is 0 or infinite, too many candidates, +inf logits) run the
 // same algorithm warp-cooperatively on full-row lists kept in a per-warp
@@ -48,9 +48,7 @@ namespace q3s {
 namespace {
 
 constexpr int MAX_WARPS = 8;
-constexpr int ARENA = 1536;       // candidate entries per warp (8 bytes each)
-constexpr int ROW_CAP = 768;      // candidates one fast row may hold
-constexpr int MAX_SLOTS = 32;     // pending rows per warp (one per lane)
+constexpr int ROW_CAP = 512;      // candidates one fast row may hold
 constexpr int FAST_MAX_K = 256;
 constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;  // bounded wait for a stage: 1 s
 
@@ -71,29 +69,19 @@ __host__ __device__ inline size_t stage_bytes(int vcap, int es) {
   return align16((size_t)vcap * es + 16);
 }
 
-// A pending fast row: its candidates are arena[off, off + c) as (x bits,
-// index); rows with top-p also own c floats after them.
-struct Slot {
-  long long row;
-  int off, c, k, n;
-  float Mx;      // row maximum of x
-  float u;       // the row's uniform draw
-  float top_p;   // top_p as f32
-  int use_top_p; // top_p < 1.0 (f64 comparison)
-};
-
 // Per-warp shared memory.
 struct FastSpace {
-  unsigned char* stage;  // raw row, TMA destination
-  uint2* arena;          // [ARENA]; the general path uses it as sort space
-  Slot* slots;           // [MAX_SLOTS]
-  uint32_t* bm;          // [vcap/32] history bitmap
-  uint32_t* hist;        // [256]
-  uint64_t* mbar;        // stage barrier
+  unsigned char* stage;     // raw row, TMA destination
+  uint2* list;              // [ROW_CAP] candidates (x bits, index)
+  float* Bb;                // [ROW_CAP] softmax terms, then running sums
+  unsigned long long* Kb;   // [ROW_CAP] sorted nucleus keys; general-path sort space
+  uint32_t* bm;             // [vcap/32] history bitmap
+  uint32_t* hist;           // [256]
+  uint64_t* mbar;           // stage barrier
 };
 
 __host__ __device__ inline size_t fast_bytes(int vcap, int es) {
-  return stage_bytes(vcap, es) + 8u * ARENA + align16(sizeof(Slot) * MAX_SLOTS) +
+  return stage_bytes(vcap, es) + 8u * ROW_CAP + 4u * ROW_CAP + 8u * ROW_CAP +
          align16(4u * (vcap / 32)) + 4u * 256 + 16u;
 }
 
@@ -102,10 +90,12 @@ __device__ inline FastSpace carve_fast(unsigned char* base, int vcap, int es) {
   size_t o = 0;
   f.stage = base;
   o += stage_bytes(vcap, es);
-  f.arena = reinterpret_cast<uint2*>(base + o);
-  o += 8u * ARENA;
-  f.slots = reinterpret_cast<Slot*>(base + o);
-  o += align16(sizeof(Slot) * MAX_SLOTS);
+  f.list = reinterpret_cast<uint2*>(base + o);
+  o += 8u * ROW_CAP;
+  f.Bb = reinterpret_cast<float*>(base + o);
+  o += 4u * ROW_CAP;
+  f.Kb = reinterpret_cast<unsigned long long*>(base + o);
+  o += 8u * ROW_CAP;
   f.bm = reinterpret_cast<uint32_t*>(base + o);
   o += align16(4u * (vcap / 32));
   f.hist = reinterpret_cast<uint32_t*>(base + o);
@@ -824,181 +814,190 @@ __device__ __forceinline__ void write_cands(const FastSpace& f, const RowCtx& r,
 }
 
 // ===========================================================================
-// Fast path: one lane finishes one row from its candidate list.
+// Fast path: warp-cooperative finish of a row from its candidate list.
 // ===========================================================================
 
 __device__ __forceinline__ float ex(const uint2& e) { return __uint_as_float(e.x); }
 __device__ __forceinline__ uint32_t kx(const uint2& e) { return total_key(__uint_as_float(e.x)); }
 
-// Shell sort gaps (Ciura's sequence).
-__constant__ int kGaps[7] = {301, 132, 57, 23, 10, 4, 1};
-
-// Shell sort of E[0..s) by index ascending, moving P along when given.
-__device__ __forceinline__ void sort_by_index(uint2* E, float* P, int s) {
-#pragma unroll 1
-  for (int gi = 0; gi < 7; ++gi) {
-    const int g = kGaps[gi];
-#pragma unroll 1
-    for (int i = g; i < s; ++i) {
-      const uint2 v = E[i];
-      const float pv = P ? P[i] : 0.0f;
-      int j = i;
-      while (j >= g && E[j - g].y > v.y) {
-        E[j] = E[j - g];
-        if (P) P[j] = P[j - g];
-        j -= g;
+// Ascending bitonic sort of 32*R keys held R per lane (element lane*R + r);
+// R is a power of two.
+template <int R, typename T>
+__device__ __forceinline__ void bitonic(T (&v)[R]) {
+  const unsigned lane = lane_id();
+#pragma unroll
+  for (int size = 2; size <= 32 * R; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (stride >= R) {
+        const int ls = stride / R;
+        const bool lower = (lane & ls) == 0;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const bool up = (((int)lane * R + r) & size) == 0;
+          const T o = __shfl_xor_sync(FULL, v[r], ls);
+          v[r] = (lower == up) ? (o < v[r] ? o : v[r]) : (o > v[r] ? o : v[r]);
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          if ((r & stride) == 0) {
+            const bool up = (((int)lane * R + r) & size) == 0;
+            const T a = v[r], b = v[r + stride];
+            if ((a > b) == up) {
+              v[r] = b;
+              v[r + stride] = a;
+            }
+          }
+        }
       }
-      E[j] = v;
-      if (P) P[j] = pv;
     }
   }
 }
 
-// Shell sort of (E, P) by (p desc, index asc).
-__device__ __forceinline__ void sort_by_prob(uint2* E, float* P, int s) {
-#pragma unroll 1
-  for (int gi = 0; gi < 7; ++gi) {
-    const int g = kGaps[gi];
-#pragma unroll 1
-    for (int i = g; i < s; ++i) {
-      const uint2 v = E[i];
-      const float pv = P[i];
-      int j = i;
-      while (j >= g && (P[j - g] < pv || (P[j - g] == pv && E[j - g].y > v.y))) {
-        E[j] = E[j - g];
-        P[j] = P[j - g];
-        j -= g;
-      }
-      E[j] = v;
-      P[j] = pv;
-    }
-  }
+// Register slot `slot` of v held by lane `owner`, broadcast.
+template <int R, typename T>
+__device__ __forceinline__ T pick(const T (&v)[R], int owner, int slot) {
+  T x = v[0];
+#pragma unroll
+  for (int r = 1; r < R; ++r)
+    if (r == slot) x = v[r];
+  return __shfl_sync(FULL, x, owner);
 }
 
-// Finishes one row from its candidates E[0..c) (x bits, index), c >= k:
-// the statements of sampling.rs:654-729 restricted to the candidate set,
-// which holds every value >= the k-th largest.  P: scratch of c floats when
-// use_top_p.  Writes the top-k threshold to *t_out.
-__device__ RowOut lane_finish(uint2* E, float* P, int c, int k, int n, float Mx, float u,
-                              bool use_top_p, float top_p, float* t_out, unsigned char* masks,
-                              float* probs) {
-  // k-th largest x: quickselect (Hoare partition, descending keys).
-  int lo = 0, hi = c - 1;
-  const int target = k - 1;
-  uint32_t tkey;
-#pragma unroll 1
-  for (;;) {
-    if (lo >= hi) {
-      tkey = kx(E[target]);
-      break;
-    }
-    const uint32_t a = kx(E[lo]), b = kx(E[(lo + hi) >> 1]), d = kx(E[hi]);
-    const uint32_t pv = max(min(a, b), min(max(a, b), d));  // median of three
-    int i = lo, j = hi;
-    while (i <= j) {
-      while (i <= hi && kx(E[i]) > pv) ++i;
-      while (j >= lo && kx(E[j]) < pv) --j;
-      if (i <= j) {
-        const uint2 tmp = E[i];
-        E[i] = E[j];
-        E[j] = tmp;
-        ++i;
-        --j;
-      }
-    }
-    if (target <= j) {
-      hi = j;
-    } else if (target >= i) {
-      lo = i;
-    } else {
-      tkey = pv;
-      break;
-    }
+__device__ __forceinline__ unsigned long long pack_out(int status, uint32_t token) {
+  return ((unsigned long long)(unsigned)status << 32) | token;
+}
+
+// Finishes a row from its candidates L[0..c) (x bits, index), k <= c <= 32*R:
+// the statements of sampling.rs:654-729 on the candidate set, which holds
+// every value >= the k-th largest.  Sort keys are 32-bit: (~total_key(x)) for
+// the selection, (index << 16 | list position) for vocabulary order.  Writes
+// the top-k threshold to tsm[0].  Kept out of line (one copy per R) with
+// scalar and pointer arguments only.
+template <int R>
+__device__ __noinline__ unsigned long long finish_warp(const uint2* L, int c, int k, int n,
+                                                      float Mx, float u, int use_top_p,
+                                                      float top_p, float* Bb,
+                                                      unsigned long long* Kb, float* tsm,
+                                                      unsigned char* masks, float* probs) {
+  constexpr uint32_t NONE = 0xFFFFFFFFu;
+  const int lane = (int)lane_id();
+  // Sort 1: x descending; the k-th largest value is at position k - 1.
+  uint32_t v[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int e = lane * R + r;
+    v[r] = e < c ? ~kx(L[e]) : NONE;
   }
-  const float t = from_total_key(tkey);
-  *t_out = t;
-  // Survivors x >= t (sampling.rs:657-662), then vocabulary order.
+  bitonic<R>(v);
+  const uint32_t tk = pick<R>(v, (k - 1) / R, (k - 1) % R);
+  const float t = from_total_key(~tk);
+  if (lane == 0) tsm[0] = t;
+  // Sort 2: survivors x >= t (sampling.rs:657-662) by vocabulary index.
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int e = lane * R + r;
+    uint32_t key = NONE;
+    if (e < c) {
+      const uint2 en = L[e];
+      if (ex(en) >= t) key = (en.y << 16) | (uint32_t)e;
+    }
+    v[r] = key;
+  }
+  bitonic<R>(v);
   int s = 0;
-  for (int j = 0; j < c; ++j)
-    if (ex(E[j]) >= t) E[s++] = E[j];
-  sort_by_index(E, nullptr, s);
+#pragma unroll
+  for (int r = 0; r < R; ++r) s += v[r] != NONE ? 1 : 0;
+  s = (int)__reduce_add_sync(FULL, (unsigned)s);
+  float xr[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) xr[r] = v[r] != NONE ? ex(L[v[r] & 0xFFFFu]) : neg_inf();
   float m2 = Mx;
   int ns = s;
   if (use_top_p) {
     // Denominator in vocabulary order (sampling.rs:666-679).
-    float total = 0.0f;
-    for (int j = 0; j < s; ++j) {
-      const float e = cr_expf(__fsub_rn(ex(E[j]), Mx));
-      P[j] = e;
-      total = __fadd_rn(total, e);
-    }
-    if (!is_finite(total) || total <= 0.0f) return {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      Bb[lane * R + r] = v[r] != NONE ? cr_expf(__fsub_rn(xr[r], Mx)) : 0.0f;
+    __syncwarp();
+    const float total = chain_sum(Bb, s, false);
+    if (!is_finite(total) || total <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
     const float inv_total = __fdiv_rn(1.0f, total);
     const float cutoff = __fsub_rn(Mx, 16.0f);
-    for (int j = 0; j < s; ++j) P[j] = ex(E[j]) >= cutoff ? __fmul_rn(P[j], inv_total) : 0.0f;
-    // Nucleus in (p desc, index asc) order (sampling.rs:690-697).
-    sort_by_prob(E, P, s);
-    float cum = 0.0f;
-    int keep = 0;
-    for (int j = 0; j < s && P[j] > 0.0f; ++j) {
-      if (j > 0 && cum >= top_p) break;
-      cum = __fadd_rn(cum, P[j]);
-      keep = j + 1;
+    // Sort 3: (p desc, index asc) over the entries within 16 of the maximum.
+    unsigned long long w[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      w[r] = ~0ull;
+      if (v[r] != NONE && xr[r] >= cutoff) {
+        const float p = __fmul_rn(Bb[lane * R + r], inv_total);
+        w[r] = ((unsigned long long)(~__float_as_uint(p)) << 32) | v[r];
+      }
     }
-    ns = keep;
-    sort_by_index(E, nullptr, ns);
+    bitonic<R>(w);
+#pragma unroll
+    for (int r = 0; r < R; ++r) Kb[lane * R + r] = w[r];
+    __syncwarp();
+    // The nucleus: positions before the first position > 0 whose preceding
+    // cumulative reaches top_p (sampling.rs:690-697).
+    int J = 0;
+    if (lane == 0) {
+      float cum = 0.0f;
+      for (int q = 0; q < 32 * R; ++q) {
+        const unsigned long long key = Kb[q];
+        if (key == ~0ull) break;
+        if (q > 0 && cum >= top_p) break;
+        cum = __fadd_rn(cum, __uint_as_float(~(uint32_t)(key >> 32)));
+        J = q + 1;
+      }
+    }
+    J = __shfl_sync(FULL, J, 0);
+    // Sort 4: the nucleus back into vocabulary order.
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = lane * R + r < J ? (uint32_t)w[r] : NONE;
+    bitonic<R>(v);
+    ns = J;
     m2 = neg_inf();
-    for (int j = 0; j < ns; ++j) m2 = fmaxf(m2, ex(E[j]));
-    if (!(m2 > neg_inf())) return {Q3S_STATUS_NO_CANDIDATE, 0u};
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      xr[r] = v[r] != NONE ? ex(L[v[r] & 0xFFFFu]) : neg_inf();
+      m2 = fmaxf(m2, xr[r]);
+    }
+    m2 = warp_max(m2);
+    if (!(m2 > neg_inf())) return pack_out(Q3S_STATUS_NO_CANDIDATE, 0u);
   }
   // Final softmax and the vocabulary-order draw (sampling.rs:700-729).
-  float sum = 0.0f;
-  for (int j = 0; j < ns; ++j) {
-    const float e = cr_expf(__fsub_rn(ex(E[j]), m2));
-    E[j].x = __float_as_uint(e);
-    sum = __fadd_rn(sum, e);
-  }
-  if (!is_finite(sum) || sum <= 0.0f) return {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+    Bb[lane * R + r] = lane * R + r < ns ? cr_expf(__fsub_rn(xr[r], m2)) : 0.0f;
+  __syncwarp();
+  const float sum = chain_sum(Bb, ns, true);
+  if (!is_finite(sum) || sum <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
   const float thr = __fmul_rn(u, sum);
-  float cum = 0.0f;
+  uint32_t first = NONE;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int e = lane * R + r;
+    if (e < ns && Bb[e] >= thr) first = min(first, (uint32_t)e);
+  }
+  first = __reduce_min_sync(FULL, first);
   uint32_t token = (uint32_t)(n - 1);
-  for (int j = 0; j < ns; ++j) {
-    cum = __fadd_rn(cum, ex(E[j]));
-    if (cum >= thr) {
-      token = E[j].y;
-      break;
-    }
-  }
+  if (first != NONE) token = pick<R>(v, (int)first / R, (int)first % R) >> 16;
   if (masks || probs) {
-    for (int j = 0; j < ns; ++j) {
-      if (masks) masks[E[j].y] |= 4;
-      if (probs) probs[E[j].y] = __double2float_rn((double)ex(E[j]) / (double)sum);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (lane * R + r < ns) {
+        const uint32_t i = v[r] >> 16;
+        if (masks) masks[i] |= 4;
+        if (probs)
+          probs[i] = __double2float_rn((double)cr_expf(__fsub_rn(xr[r], m2)) / (double)sum);
+      }
     }
   }
-  return {Q3S_STATUS_OK, token};
-}
-
-// Every lane finishes the pending row of its slot.
-__device__ __forceinline__ void flush_slots(const KernelArgs& a, const FastSpace& f, int nslots) {
   __syncwarp();
-  const int b = (int)lane_id();
-  if (b < nslots) {
-    const Slot sl = f.slots[b];
-    uint2* E = f.arena + sl.off;
-    float t;
-    const RowOut o = lane_finish(E, reinterpret_cast<float*>(E + sl.c), sl.c, sl.k, sl.n, sl.Mx,
-                                 sl.u, sl.use_top_p != 0, sl.top_p, &t, nullptr, nullptr);
-    a.tokens[sl.row] = o.token;
-    a.status[sl.row] = (unsigned char)o.status;
-  }
-  __syncwarp();
+  return pack_out(Q3S_STATUS_OK, token);
 }
-
-// Pending-row bookkeeping of a warp.
-struct Batch {
-  int nslots;
-  int used;  // arena entries in use
-};
 
 // Debug pass over the stage: bit0 finite x, bit1 x >= t (OR-ed in).
 template <int DT, bool XF>
@@ -1015,35 +1014,31 @@ __device__ void debug_masks(const FastSpace& f, const RowCtx& r, float t, unsign
   __syncwarp();
 }
 
-enum { FAST_PENDING = 0, FAST_DONE = 1, FAST_GENERAL = 2 };
-
-// Scans the staged row and appends its candidates as a pending slot.
-// FAST_PENDING: slot recorded, stage released.  FAST_DONE: `out` holds the
-// result, stage released.  FAST_GENERAL: the row needs the general path; the
-// stage is still held.
+// Fast path.  Returns false (before releasing the stage) when the row must
+// take the general path instead.
 template <int DT, int NJ, bool XF, bool EDGE>
-__device__ int fast_row(const KernelArgs& a, const FastSpace& f, const StageView& s,
-                        const RowMeta& m, const RowCtx& rc, float u, long long row, Releaser& rel,
-                        float& delta, Batch& batch, RowOut& out, const DebugRow& dbg) {
+__device__ bool fast_row(const FastSpace& f, const StageView& s, const RowMeta& m,
+                         const RowCtx& rc, float u, Releaser& rel, float& delta, RowOut& out,
+                         const DebugRow& dbg) {
   const q3s_row_params& P = m.P;
   float vm[NJ];
   const float mx = scan_stage<DT, NJ, XF, EDGE>(f, rc, vm);
-  if (!XF && mx == __int_as_float(0x7f800000)) return FAST_GENERAL;  // raw +inf
+  if (!XF && mx == __int_as_float(0x7f800000)) return false;  // raw +inf
   if (mx == neg_inf() || mx != mx) {
     release<DT>(rel);
     out = {rc.sf >= 0 ? Q3S_STATUS_SUPPRESSION_NO_CANDIDATE : Q3S_STATUS_NO_CANDIDATE, 0u};
-    return FAST_DONE;
+    return true;
   }
   const float Mx = XF ? mx : __fmul_rn(mx, rc.inv);
   if (Mx == __int_as_float(0x7f800000)) {
     release<DT>(rel);
     out = {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
-    return FAST_DONE;
+    return true;
   }
   const int k = (int)P.top_k;
   const int hi = k <= 128 ? max(2 * k, 64) : k + 96;
   float tau;
-  if (!find_tau(vm, mx, k, hi, delta, tau)) return FAST_GENERAL;
+  if (!find_tau(vm, mx, k, hi, delta, tau)) return false;
   // Raw-domain selection: lower tau until its image lies strictly below the
   // image of tau, so no element below the new tau can tie the k-th largest
   // x after the multiply.
@@ -1056,7 +1051,7 @@ __device__ int fast_row(const KernelArgs& a, const FastSpace& f, const StageView
       t2 = __fsub_rn(t2, fmaxf(fabsf(t2) * 3.814697265625e-06f, 1.1754944e-38f));
       ok = __fmul_rn(t2, rc.inv) < img;
     }
-    if (!ok) return FAST_GENERAL;
+    if (!ok) return false;
     tau = t2;
   }
   uint64_t flags = 0;
@@ -1065,54 +1060,30 @@ __device__ int fast_row(const KernelArgs& a, const FastSpace& f, const StageView
   const int mine = count_cands<DT, XF, EDGE>(f, rc, flags, tau);
   const int incl = (int)warp_inclusive_scan((uint32_t)mine);
   const int c = __shfl_sync(FULL, incl, 31);
-  if (c < k || c > ROW_CAP) return FAST_GENERAL;
-  const bool use_top_p = P.top_p < 1.0;
-  const int need = c + (use_top_p ? (c + 1) / 2 : 0);
-  if (batch.used + need > ARENA || dbg.masks) {
-    flush_slots(a, f, batch.nslots);
-    batch.nslots = 0;
-    batch.used = 0;
-  }
-  uint2* base = f.arena + batch.used;
-  write_cands<DT, XF, EDGE>(f, rc, flags, tau, base + (incl - mine));
+  if (c < k || c > ROW_CAP) return false;
+  write_cands<DT, XF, EDGE>(f, rc, flags, tau, f.list + (incl - mine));
   __syncwarp();
+  if (!dbg.masks) release<DT>(rel);
+  const int use_top_p = P.top_p < 1.0 ? 1 : 0;
+  const float top_p = (float)P.top_p;
+  float* tsm = reinterpret_cast<float*>(f.hist);
+  unsigned long long r;
+  if (c <= 32)
+    r = finish_warp<1>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, f.Bb, f.Kb, tsm, dbg.masks,
+                       dbg.probs);
+  else if (c <= 128)
+    r = finish_warp<4>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, f.Bb, f.Kb, tsm, dbg.masks,
+                       dbg.probs);
+  else
+    r = finish_warp<16>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, f.Bb, f.Kb, tsm, dbg.masks,
+                        dbg.probs);
+  out = {(int)(r >> 32), (uint32_t)r};
   if (dbg.masks) {
-    // Debug rows finish at once (lane 0) while the stage is still held.
-    float t = 0.0f;
-    RowOut o{0, 0u};
-    if (lane_id() == 0)
-      o = lane_finish(base, reinterpret_cast<float*>(base + c), c, k, s.n, Mx, u, use_top_p,
-                      (float)P.top_p, &t, dbg.masks, dbg.probs);
     __syncwarp();
-    t = __shfl_sync(FULL, t, 0);
-    o.status = __shfl_sync(FULL, o.status, 0);
-    o.token = __shfl_sync(FULL, o.token, 0);
-    debug_masks<DT, XF>(f, rc, t, dbg.masks);
+    debug_masks<DT, XF>(f, rc, tsm[0], dbg.masks);
     release<DT>(rel);
-    out = o;
-    return FAST_DONE;
   }
-  release<DT>(rel);
-  if (lane_id() == 0) {
-    Slot& sl = f.slots[batch.nslots];
-    sl.row = row;
-    sl.off = batch.used;
-    sl.c = c;
-    sl.k = k;
-    sl.n = s.n;
-    sl.Mx = Mx;
-    sl.u = u;
-    sl.top_p = (float)P.top_p;
-    sl.use_top_p = use_top_p ? 1 : 0;
-  }
-  batch.nslots += 1;
-  batch.used += need;
-  if (batch.nslots == MAX_SLOTS) {
-    flush_slots(a, f, batch.nslots);
-    batch.nslots = 0;
-    batch.used = 0;
-  }
-  return FAST_PENDING;
+  return true;
 }
 
 // Greedy row (sampling.rs:574-591) straight from the stage.
@@ -1139,13 +1110,11 @@ __device__ RowOut greedy_stage(const FastSpace& f, const StageView& s, int sf, i
   return {Q3S_STATUS_OK, 0xFFFFFFFFu - (uint32_t)best};
 }
 
-// A sampled row: fast path when it applies, else the general path (after the
-// warp's pending rows are finished, since the general path borrows the arena).
-// Returns false when the row is pending in the batch.
+// A sampled row: fast path when it applies, else the general path.
 template <int DT, int NJ>
-__device__ bool sampled_row(const KernelArgs& a, const FastSpace& f, const GenSpace& g,
-                            const RowMeta& m, const StageView& s, long long row, Releaser& rel,
-                            float& delta, Batch& batch, RowOut& out, const DebugRow& dbg) {
+__device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const GenSpace& g,
+                              const RowMeta& m, const StageView& s, Releaser& rel, float& delta,
+                              const DebugRow& dbg) {
   const q3s_row_params& P = m.P;
   RowCtx rc;
   rc.n = s.n;
@@ -1164,29 +1133,25 @@ __device__ bool sampled_row(const KernelArgs& a, const FastSpace& f, const GenSp
   if (fast) {
     const bool xf = rc.use_pen || rc.sf >= 0;
     const bool edge = s.mis != 0 || (s.n % Elem<DT>::EPV) != 0;
-    int r;
+    RowOut out;
+    bool done;
     if (xf)
-      r = edge ? fast_row<DT, NJ, true, true>(a, f, s, m, rc, u, row, rel, delta, batch, out, dbg)
-               : fast_row<DT, NJ, true, false>(a, f, s, m, rc, u, row, rel, delta, batch, out, dbg);
+      done = edge ? fast_row<DT, NJ, true, true>(f, s, m, rc, u, rel, delta, out, dbg)
+                  : fast_row<DT, NJ, true, false>(f, s, m, rc, u, rel, delta, out, dbg);
     else
-      r = edge ? fast_row<DT, NJ, false, true>(a, f, s, m, rc, u, row, rel, delta, batch, out, dbg)
-               : fast_row<DT, NJ, false, false>(a, f, s, m, rc, u, row, rel, delta, batch, out, dbg);
-    if (r == FAST_PENDING) return false;
-    if (r == FAST_DONE) return true;
+      done = edge ? fast_row<DT, NJ, false, true>(f, s, m, rc, u, rel, delta, out, dbg)
+                  : fast_row<DT, NJ, false, false>(f, s, m, rc, u, rel, delta, out, dbg);
+    if (done) return out;
   }
-  flush_slots(a, f, batch.nslots);
-  batch.nslots = 0;
-  batch.used = 0;
   const unsigned lane = lane_id();
   for (int i = lane; i < s.n; i += 32) g.A[i] = stage_elem<DT>(f.stage, s.mis, i);
   __syncwarp();
   release<DT>(rel);
   const unsigned long long r = general_compute(
-      g.A, g.B, g.BX, g.BI, f.bm, f.hist, reinterpret_cast<unsigned long long*>(f.arena), s.n,
+      g.A, g.B, g.BX, g.BI, f.bm, f.hist, f.Kb, s.n,
       rc.inv, rc.pf, rc.use_pen ? 1 : 0, rc.sf, rc.allow, P.top_k, P.top_p, u, dbg.masks,
       dbg.probs);
-  out = {(int)(r >> 32), (uint32_t)r};
-  return true;
+  return {(int)(r >> 32), (uint32_t)r};
 }
 
 template <int DT, int NJ>
@@ -1210,7 +1175,6 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
   if (row < a.num_rows && lane == 0) issue_row<DT>(a, row, f);
   uint32_t phase = 0;
   float delta = 0.0f;
-  Batch batch{0, 0};
   // Per-row metadata is loaded one row ahead so its latency overlaps a row.
   RowMeta cur;
   if (row < a.num_rows) cur = load_meta(a, row);
@@ -1243,9 +1207,8 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
     const bool ready = mbar_wait_bounded(f.mbar, phase, WAIT_LIMIT_NS);
     phase ^= 1u;
     if (!ready) {
-      // The stage never arrived: finish what is pending, mark this warp's
-      // remaining rows and stop after another bounded wait for the copy.
-      flush_slots(a, f, batch.nslots);
+      // The stage never arrived: mark this warp's remaining rows and stop
+      // after another bounded wait for the copy in flight.
       mbar_wait_bounded(f.mbar, phase ^ 1u, WAIT_LIMIT_NS);
       for (long long r = row; r < a.num_rows; r += stride)
         if (lane == 0) {
@@ -1255,24 +1218,22 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
       return;
     }
     RowOut out{st, 0u};
-    bool have = true;
     if (st == Q3S_STATUS_OK) {
       const StageView s = complete_stage<DT>(a, row, n, f);
       if (!P.do_sample) {
         out = greedy_stage<DT>(f, s, P.suppress_from, P.allow_token);
       } else {
-        have = sampled_row<DT, NJ>(a, f, g, cur, s, row, rel, delta, batch, out, dbg);
+        out = sampled_row<DT, NJ>(a, f, g, cur, s, rel, delta, dbg);
       }
     }
     release<DT>(rel);
-    if (have && lane == 0) {
+    if (lane == 0) {
       a.tokens[row] = out.token;
       a.status[row] = (unsigned char)out.status;
     }
     __syncwarp();
     cur = nxt;
   }
-  flush_slots(a, f, batch.nslots);
 }
 
 // Greedy argmax rows (sampling.rs:40-60 and :72-117), one warp per row.
