@@ -141,6 +141,25 @@ void q3s_context_destroy(q3s_context* ctx);
  * caller advances subseq for rows whose status is OK and do_sample is set. */
 int q3s_sample_batch(q3s_context* ctx, const q3s_batch* batch, void* stream);
 
+/* Bytes of the file-scope device workspace of q3s_sample_batch_static, held on
+ * every device that loads the library until the process exits. */
+#define Q3S_STATIC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
+/* q3s_sample_batch without any device allocation: the same kernel, with its
+ * general-path workspace in a file-scope device array of
+ * Q3S_STATIC_SCRATCH_BYTES instead of a context allocation.  No counterpart
+ * in the reference, which samples on the host (src/talker/sampling.rs) and
+ * keeps no device workspace.  Same arguments and results as
+ * q3s_sample_batch; in addition it rejects vocab > Q3S_MAX_VOCAB with
+ * Q3S_E_INVALID_ARGUMENT, and it launches only as many blocks as the array
+ * holds workspace for (about 14 bytes per vocabulary entry per warp, 8 warps
+ * a block: 146 blocks at vocab 2048, 97 at 3072, 73 at 4096).  The first call on
+ * a device looks up the array's address (cudaGetSymbolAddress, which may load
+ * the module): make it before any stream capture.  Calls share the array and
+ * nothing in it has to start at zero; calls whose kernels overlap on the GPU
+ * race on it, so order them on one stream or with events. */
+int q3s_sample_batch_static(q3s_context* ctx, const q3s_batch* batch, void* stream);
+
 /* Greedy argmax with the talker reserved-token mask, many rows, on device.
  * mode Q3S_GREEDY_SELECT follows greedy_select (sampling.rs:40-60): first
  * index of the IEEE maximum over finite allowed entries; status

@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include "../../include/q3s_sampler.h"
+#include "q3s_internal.h"
 #include "q3s_kernels.h"
 
 namespace {
@@ -76,6 +77,18 @@ struct q3s_sampler {
   uint32_t ctr_lo;
   q3s_sampler_diagnostics diag;
 };
+
+namespace q3s {
+
+ContextInfo context_info(const q3s_context* ctx) {
+  return ContextInfo{ctx->device, ctx->sm_count, ctx->smem_optin};
+}
+
+int record_error(int code, const std::string& msg) { return fail(code, msg); }
+
+int record_cuda_error(cudaError_t e, const char* what) { return cuda_fail(e, what); }
+
+}  // namespace q3s
 
 extern "C" {
 

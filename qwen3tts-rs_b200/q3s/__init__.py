@@ -107,7 +107,7 @@ EXPORTED_SYMBOLS = (
     "q3s_context_destroy", "q3s_sample_batch", "q3s_greedy_batch", "q3s_sampler_create",
     "q3s_sampler_destroy", "q3s_sampler_subsequence_counter",
     "q3s_sampler_set_subsequence_counter", "q3s_sampler_get_diagnostics",
-    "q3s_sampler_sample_with_mode", "q3s_sampler_sample",
+    "q3s_sampler_sample_with_mode", "q3s_sampler_sample", "q3s_sample_batch_static",
 )
 
 _lib = None
@@ -137,6 +137,8 @@ def load(path: Optional[os.PathLike] = None):
     L.q3s_context_destroy.argtypes = [ctypes.c_void_p]
     L.q3s_context_destroy.restype = None
     L.q3s_sample_batch.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Batch), ctypes.c_void_p]
+    L.q3s_sample_batch_static.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Batch),
+                                          ctypes.c_void_p]
     L.q3s_greedy_batch.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
@@ -268,6 +270,30 @@ def sample_batch(logits, params, seeds=None, subseqs=None, *, row_offsets=None, 
     history_offsets [R+1] int64.  Returns (tokens int32 [R], status uint8 [R])
     and, with debug=True, also (probs [R, V] float32, masks [R, V] uint8).
     """
+    return _launch_batch("q3s_sample_batch", logits, params, seeds, subseqs,
+                         row_offsets=row_offsets, row_vocab=row_vocab, vocab=vocab,
+                         history=history, history_offsets=history_offsets,
+                         uniform_override=uniform_override, debug=debug, ctx=ctx, stream=stream,
+                         out=out)
+
+
+def sample_batch_static(logits, params, seeds=None, subseqs=None, *, row_offsets=None,
+                        row_vocab=None, vocab: Optional[int] = None, history=None,
+                        history_offsets=None, uniform_override=None, debug: bool = False,
+                        ctx: Optional[Context] = None, stream=None, out=None):
+    """sample_batch through q3s_sample_batch_static: the same launch with the
+    library's file-scope device workspace, so the call itself allocates
+    nothing on the device (pass `out` to keep torch from allocating the
+    outputs).  Rejects vocab > MAX_VOCAB."""
+    return _launch_batch("q3s_sample_batch_static", logits, params, seeds, subseqs,
+                         row_offsets=row_offsets, row_vocab=row_vocab, vocab=vocab,
+                         history=history, history_offsets=history_offsets,
+                         uniform_override=uniform_override, debug=debug, ctx=ctx, stream=stream,
+                         out=out)
+
+
+def _launch_batch(entry: str, logits, params, seeds, subseqs, *, row_offsets, row_vocab, vocab,
+                  history, history_offsets, uniform_override, debug, ctx, stream, out):
     import torch
     dev = logits.device
     if logits.dtype == torch.float32:
@@ -325,8 +351,7 @@ def sample_batch(logits, params, seeds=None, subseqs=None, *, row_offsets=None, 
     b.masks = _dptr(masks)
     b.probs_stride = V if debug else 0
     s = torch.cuda.current_stream(dev).cuda_stream if stream is None else stream
-    _check(load().q3s_sample_batch(ctx.handle, ctypes.byref(b), ctypes.c_void_p(s)),
-           "q3s_sample_batch")
+    _check(getattr(load(), entry)(ctx.handle, ctypes.byref(b), ctypes.c_void_p(s)), entry)
     if debug:
         return tokens, status, probs, masks
     return tokens, status
