@@ -36,9 +36,11 @@ TOP_K = 50
 # Algorithmic bytes per row of the bandwidth workload: 3072 f32 logits,
 # the Philox seed and subsequence (8 + 8), the token (4) and the status (1).
 BYTES_PER_ROW = 4 * VOCAB + 16 + 4 + 1
-# DRAM bytes per launch of the sampling kernel from the ncu capture summarised
-# in profiles/sample_kernel_bandwidth_65536x3072.md (None until captured).
-NCU_TRAFFIC_PER_LAUNCH = None
+# DRAM bytes (read + write) per 65,536-row launch of the sampling kernel: the
+# ncu capture of a 16,384-row launch (207.4 MB, summarised in
+# profiles/sample_kernel_bandwidth_16384x3072_k50_full.md) scaled by the rows,
+# since every row is read exactly once.
+NCU_TRAFFIC_PER_LAUNCH = 207.427072e6 * 4
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -204,11 +206,12 @@ def run_reference(args, world, rank):
     return 0
 
 
-def workload_config():
-    return {"workload": "bandwidth: 65536 rows x 3072 f32 logits ~N(0,1) per GPU, top_k 50, "
+def workload_config(rows: int = ROWS):
+    mb = rows * 4 * VOCAB / 1e6
+    return {"workload": f"bandwidth: {rows} rows x 3072 f32 logits ~N(0,1) per GPU, top_k 50, "
                         "top_p 1.0, temperature 1.0, no penalty",
-            "rows_per_gpu": ROWS, "vocab": VOCAB, "top_k": TOP_K, "global_batch": None,
-            "l2": "inputs 805 MB per step > 126 MB L2 (no flush needed)",
+            "rows_per_gpu": rows, "vocab": VOCAB, "top_k": TOP_K, "global_batch": None,
+            "l2": f"inputs {mb:.0f} MB per step > 126 MB L2 (no flush needed)",
             "parallelism": "row shards, no collective"}
 
 
@@ -220,17 +223,20 @@ def main() -> int:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--rows", type=int, default=ROWS,
+                    help="rows per GPU (smaller cases are for profiler captures only)")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     if args.impl == "reference":
         return run_reference(args, world, rank)
+    rows = args.rows
 
     import numpy as np
     import torch
     import torch.distributed as dist
 
     import q3s
-    from q3s import workloads
+    from q3s import shard, workloads
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -244,18 +250,14 @@ def main() -> int:
             dist.barrier()
 
     def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return shard.max_over_ranks(v, device=dev)
 
     ctx = q3s.Context(local)
-    w = workloads.bandwidth(dev, rows=ROWS, top_k=TOP_K, seed=3 + rank)
+    w = workloads.bandwidth(dev, rows=rows, top_k=TOP_K, seed=3 + rank)
     a = w.device_args(dev)
     params, seeds, subseqs = a["params"], a["seeds"], a["subseqs"]
-    tokens = torch.empty(ROWS, dtype=torch.int32, device=dev)
-    status = torch.empty(ROWS, dtype=torch.uint8, device=dev)
+    tokens = torch.empty(rows, dtype=torch.int32, device=dev)
+    status = torch.empty(rows, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
     def launch():
@@ -285,24 +287,24 @@ def main() -> int:
     elapsed_ms = max_over_ranks(t_begin.elapsed_time(t_end))
     kernel_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / max(args.steps, 1)
     kernel_ms = max_over_ranks(kernel_ms)
-    value = world * ROWS * args.steps / (elapsed_ms / 1e3)
+    value = shard.whole_job_rate(rows, world, args.steps, elapsed_ms)
     peak, peak_kind = measured_peak_gbs()
-    achieved = ROWS * BYTES_PER_ROW / (kernel_ms / 1e3) / 1e9
+    achieved = rows * BYTES_PER_ROW / (kernel_ms / 1e3) / 1e9
 
     # End to end through the C ABI with host buffers.
     e2e = None
     if args.e2e_steps > 0:
-        host_logits = torch.empty((ROWS, VOCAB), dtype=torch.float32, pin_memory=True)
+        host_logits = torch.empty((rows, VOCAB), dtype=torch.float32, pin_memory=True)
         host_logits.copy_(w.logits)
         host_seeds = seeds.cpu().pin_memory()
         host_sub = subseqs.cpu().pin_memory()
-        host_tok = torch.empty(ROWS, dtype=torch.int32, pin_memory=True)
-        host_st = torch.empty(ROWS, dtype=torch.uint8, pin_memory=True)
+        host_tok = torch.empty(rows, dtype=torch.int32, pin_memory=True)
+        host_st = torch.empty(rows, dtype=torch.uint8, pin_memory=True)
         dev_logits = torch.empty_like(w.logits)
         dev_seeds = torch.empty_like(seeds)
         dev_sub = torch.empty_like(subseqs)
         chunks = 8
-        cr = ROWS // chunks
+        cr = rows // chunks
         streams = [torch.cuda.Stream(dev) for _ in range(2)]
 
         def e2e_step():
@@ -338,9 +340,9 @@ def main() -> int:
         e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.e2e_steps
         if not bool((host_st == 0).all()):
             raise RuntimeError("end-to-end sampling failed")
-        e2e = {"value": world * ROWS / (e2e_ms / 1e3), "unit": "rows/s",
-               "h2d_bytes_per_step": ROWS * (4 * VOCAB + 16),
-               "d2h_bytes_per_step": ROWS * 5, "ms_per_step": e2e_ms}
+        e2e = {"value": world * rows / (e2e_ms / 1e3), "unit": "rows/s",
+               "h2d_bytes_per_step": rows * (4 * VOCAB + 16),
+               "d2h_bytes_per_step": rows * 5, "ms_per_step": e2e_ms}
         del host_logits, dev_logits
 
     results = {}
@@ -363,10 +365,11 @@ def main() -> int:
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": dict(workload_config(), global_batch=ROWS * world),
+            "config": dict(workload_config(rows), global_batch=rows * world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": NCU_TRAFFIC_PER_LAUNCH,
+                         "traffic": NCU_TRAFFIC_PER_LAUNCH * rows / ROWS,
+                         "traffic_unit": "bytes per launch (ncu, scaled from 16384 rows)",
                          "bytes_per_row": BYTES_PER_ROW, "kernel_ms": kernel_ms},
             "cpu_baseline": cpu,
             "e2e": e2e,
