@@ -65,8 +65,18 @@ struct Elem<Q3S_DTYPE_BF16> {
 
 __host__ __device__ inline size_t align16(size_t b) { return (b + 15) & ~size_t(15); }
 
+// 16-byte vectors per lane chunk of the fast-path scan for a row capacity:
+// ceil(vcap * es / 512) rounded up to a multiple of 8.
+__host__ __device__ constexpr int chunk_vectors(int vcap, int es) {
+  return (((vcap * es + 511) / 512) + 7) & ~7;
+}
+
+// The stage holds a row with up to 15 bytes of leading misalignment, and at
+// least the 32 lane chunks the fast-path scan reads.
 __host__ __device__ inline size_t stage_bytes(int vcap, int es) {
-  return align16((size_t)vcap * es + 16);
+  const size_t row = align16((size_t)vcap * es + 16);
+  const size_t chunks = (size_t)512 * chunk_vectors(vcap, es);
+  return row > chunks ? row : chunks;
 }
 
 // Per-warp shared memory.
@@ -220,8 +230,7 @@ __device__ StageView complete_stage(const KernelArgs& a, long long row, int n, c
 }
 
 template <int DT>
-__device__ __forceinline__ void unpack(const unsigned char* stage, int q, float (&e)[Elem<DT>::EPV]) {
-  const uint4 v = *reinterpret_cast<const uint4*>(stage + 16 * q);
+__device__ __forceinline__ void unpack_vec(const uint4& v, float (&e)[Elem<DT>::EPV]) {
   if (DT == Q3S_DTYPE_F32) {
     e[0] = __uint_as_float(v.x);
     e[1] = __uint_as_float(v.y);
@@ -235,6 +244,11 @@ __device__ __forceinline__ void unpack(const unsigned char* stage, int q, float 
       e[2 * t + 1] = __uint_as_float(w[t] & 0xFFFF0000u);
     }
   }
+}
+
+template <int DT>
+__device__ __forceinline__ void unpack(const unsigned char* stage, int q, float (&e)[Elem<DT>::EPV]) {
+  unpack_vec<DT>(*reinterpret_cast<const uint4*>(stage + 16 * q), e);
 }
 
 template <int DT>
@@ -706,26 +720,49 @@ __device__ __forceinline__ void release(Releaser& r) {
   }
 }
 
-// Vector maxima of the stage (registers) and the row maximum.
+// Vector maxima of the stage (registers) and the row maximum.  Lane l owns
+// the contiguous chunk of NJ 16-byte vectors [l*NJ, (l+1)*NJ), so chunks
+// follow vocabulary order.  Step j reads chunk vector j ^ (l & 7): the 8
+// lanes of each shared-memory phase then hit 8 distinct bank groups (NJ is a
+// multiple of 8, so the XOR permutes the chunk), and every address is one of
+// 8 per-lane bases plus an immediate offset.  vm[j] is the maximum of that
+// vector.  Vectors past the row hold stale bytes; EDGE rows mask them by
+// index.
 template <int DT, int NJ, bool XF, bool EDGE>
 __device__ __forceinline__ float scan_stage(const FastSpace& f, const RowCtx& r, float (&vm)[NJ]) {
   constexpr int EPV = Elem<DT>::EPV;
   const int lane = (int)lane_id();
+  const int sw = lane & 7;
+  const uint4* chunk = reinterpret_cast<const uint4*>(f.stage) + lane * NJ;
   float mx = neg_inf();
 #pragma unroll
   for (int j = 0; j < NJ; ++j) {
-    const int q = lane + 32 * j;
+    const int v = (j & ~7) | ((j & 7) ^ sw);
+    const uint4 w = chunk[v];
+    float e[EPV];
+    unpack_vec<DT>(w, e);
     float m = neg_inf();
-    if (q < r.Q) {
-      float e[EPV];
-      unpack<DT>(f.stage, q, e);
 #pragma unroll
-      for (int c = 0; c < EPV; ++c) m = fmaxf(m, xform<XF, EDGE>(e[c], q * EPV + c - r.mis, r));
-    }
+    for (int c = 0; c < EPV; ++c)
+      m = fmaxf(m, xform<XF, EDGE>(e[c], (lane * NJ + v) * EPV + c - r.mis, r));
     vm[j] = m;
     mx = fmaxf(mx, m);
   }
   return warp_max(mx);
+}
+
+// Bit v set when chunk vector v of this lane has its maximum >= tau.
+template <int NJ>
+__device__ __forceinline__ uint32_t chunk_flags(const float (&vm)[NJ], float tau) {
+  uint32_t F = 0;
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) F |= (vm[j] >= tau ? 1u : 0u) << j;
+  // Bit j stands for chunk vector j ^ sw: permute bit positions by XOR.
+  const int sw = (int)lane_id() & 7;
+  if (sw & 1) F = ((F & 0x55555555u) << 1) | ((F >> 1) & 0x55555555u);
+  if (sw & 2) F = ((F & 0x33333333u) << 2) | ((F >> 2) & 0x33333333u);
+  if (sw & 4) F = ((F & 0x0F0F0F0Fu) << 4) | ((F >> 4) & 0x0F0F0F0Fu);
+  return F;
 }
 
 template <int NJ>
@@ -757,7 +794,9 @@ __device__ bool find_tau(const float (&vm)[NJ], float mx, int k, int hi, float& 
       dhi = d;
       d = 0.5f * (lo + dhi);
     } else {
-      delta = d;
+      // Accepted: the next row starts from d nudged toward the middle of
+      // the window.
+      delta = 2 * c < k + hi ? __fmul_rn(d, 1.03125f) : __fmul_rn(d, 0.96875f);
       tau = t;
       return true;
     }
@@ -770,47 +809,66 @@ __device__ bool find_tau(const float (&vm)[NJ], float mx, int k, int hi, float& 
   return tau > neg_inf();
 }
 
-// Number of this lane's candidates {x >= tau} in its flagged vectors.
-template <int DT, bool XF, bool EDGE>
-__device__ __forceinline__ int count_cands(const FastSpace& f, const RowCtx& r, uint64_t flags,
-                                           float tau) {
+// The candidates {x >= tau} of the flagged vectors, in vocabulary order, as
+// (x after the temperature, index) into L.  The flagged vectors are first
+// listed warp-wide (lane-major = vocabulary order) in Qs, then processed 32
+// at a time, one per lane, with ballot prefix counts placing each lane's
+// candidates.  Returns the number of candidates, or -1 when there are more
+// than ROW_CAP.
+template <int DT, int NJ, bool XF, bool EDGE>
+__device__ __forceinline__ int collect_cands(const FastSpace& f, const RowCtx& r, uint32_t flags,
+                                             float tau, uint16_t* Qs, uint2* L) {
   constexpr int EPV = Elem<DT>::EPV;
   const int lane = (int)lane_id();
-  int cnt = 0;
-  while (flags) {
-    const int j = __ffsll((long long)flags) - 1;
-    flags &= flags - 1;
-    const int q = lane + 32 * j;
-    float e[EPV];
-    unpack<DT>(f.stage, q, e);
-#pragma unroll
-    for (int c = 0; c < EPV; ++c) cnt += xform<XF, EDGE>(e[c], q * EPV + c - r.mis, r) >= tau ? 1 : 0;
-  }
-  return cnt;
-}
-
-// Writes this lane's candidates as (x after the temperature, index).
-template <int DT, bool XF, bool EDGE>
-__device__ __forceinline__ void write_cands(const FastSpace& f, const RowCtx& r, uint64_t flags,
-                                            float tau, uint2* dst) {
-  constexpr int EPV = Elem<DT>::EPV;
-  const int lane = (int)lane_id();
-  int t = 0;
-  while (flags) {
-    const int j = __ffsll((long long)flags) - 1;
-    flags &= flags - 1;
-    const int q = lane + 32 * j;
-    float e[EPV];
-    unpack<DT>(f.stage, q, e);
-#pragma unroll
-    for (int c = 0; c < EPV; ++c) {
-      const float x = xform<XF, EDGE>(e[c], q * EPV + c - r.mis, r);
-      if (x >= tau) {
-        const float xv = XF ? x : __fmul_rn(x, r.inv);
-        dst[t++] = make_uint2(__float_as_uint(xv), (uint32_t)(q * EPV + c - r.mis));
-      }
+  const int nf = __popc(flags);
+  const int incl = (int)warp_inclusive_scan((uint32_t)nf);
+  const int NF = __shfl_sync(FULL, incl, 31);
+  {
+    int p = incl - nf;
+    uint32_t fl = flags;
+    while (fl) {
+      Qs[p++] = (uint16_t)(lane * NJ + __ffs(fl) - 1);
+      fl &= fl - 1;
     }
   }
+  __syncwarp();
+  const uint32_t lt = lanemask_lt();
+  int base = 0;
+  for (int i0 = 0; i0 < NF; i0 += 32) {
+    const int i = i0 + lane;
+    float x[EPV];
+    uint32_t bits = 0;
+    int q = 0;
+    if (i < NF) {
+      q = Qs[i];
+      float e[EPV];
+      unpack<DT>(f.stage, q, e);
+#pragma unroll
+      for (int c = 0; c < EPV; ++c) {
+        x[c] = xform<XF, EDGE>(e[c], q * EPV + c - r.mis, r);
+        bits |= (x[c] >= tau ? 1u : 0u) << c;
+      }
+    }
+    const int cnt = __popc(bits);
+    // Exclusive prefix of cnt (0..EPV) over the lanes from its binary digits.
+    int pre = 0, tot = 0;
+#pragma unroll
+    for (int d = 0; (1 << d) <= EPV; ++d) {
+      const uint32_t b = __ballot_sync(FULL, (cnt >> d) & 1);
+      pre += __popc(b & lt) << d;
+      tot += __popc(b) << d;
+    }
+    if (base + tot > ROW_CAP) return -1;
+    int o = base + pre;
+#pragma unroll
+    for (int c = 0; c < EPV; ++c)
+      if (bits & (1u << c))
+        L[o++] = make_uint2(__float_as_uint(XF ? x[c] : __fmul_rn(x[c], r.inv)),
+                            (uint32_t)(q * EPV + c - r.mis));
+    base += tot;
+  }
+  __syncwarp();
+  return base;
 }
 
 // ===========================================================================
@@ -999,6 +1057,170 @@ __device__ __noinline__ unsigned long long finish_warp(const uint2* L, int c, in
   return pack_out(Q3S_STATUS_OK, token);
 }
 
+// Bucket of x in [lo, lo + 64/scale) for the k-th-value histogram: a
+// monotone map of x (equal values share a bucket), clamped to [0, 63].
+__device__ __forceinline__ int kbucket(float x, float lo, float scale) {
+  const float y = __fmul_rn(__fsub_rn(x, lo), scale);
+  // NaN (0 * inf) and y <= 0 go to bucket 0; truncation of y in (0, 63) is
+  // its floor.
+  return y > 0.0f ? (y >= 63.0f ? 63 : (int)y) : 0;
+}
+
+// Sequential f32 prefix sums of B[0..count) in place by lane 0 (B 16-byte
+// aligned and zero-padded to a multiple of 4); returns the total to every
+// lane.  Loads run one vector ahead of the additions.
+__device__ __forceinline__ float chain_prefix(float* B, int count) {
+  float c = 0.0f;
+  if (lane_id() == 0) {
+    float4* B4 = reinterpret_cast<float4*>(B);
+    const int n4 = (count + 3) >> 2;
+    float4 nx = n4 > 0 ? B4[0] : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < n4; ++q) {
+      float4 v = nx;
+      if (q + 1 < n4) nx = B4[q + 1];
+      c = __fadd_rn(c, v.x);
+      v.x = c;
+      c = __fadd_rn(c, v.y);
+      v.y = c;
+      c = __fadd_rn(c, v.z);
+      v.z = c;
+      c = __fadd_rn(c, v.w);
+      v.w = c;
+      B4[q] = v;
+    }
+  }
+  __syncwarp();
+  return __shfl_sync(FULL, c, 0);
+}
+
+// Finishes a row without top-p from its candidates L[0..c) in vocabulary
+// order (x after the temperature, index), k <= c: the statements of
+// sampling.rs:654-663 and 700-729 on the candidate set, which holds every
+// element >= the k-th largest x (all others are masked by top-k).
+//   * t, the k-th largest x (ties kept): a 64-bucket histogram of the
+//     candidates over [lo, Mx] locates the bucket holding the k-th largest;
+//     the few values in that bucket are ranked exactly.
+//   * The survivors x >= t, still in vocabulary order, get exp(x - Mx)
+//     (masked entries are exact zeros of the reference's sums and are
+//     skipped); one lane accumulates the sequential f32 prefix sums, and the
+//     draw is the first survivor whose running sum reaches u * sum.
+// Returns pack_out(status, token); returns pack_out(NOT_RUN, 0) when the
+// bucket of the k-th value holds more than 32 candidates (the caller then
+// uses the sorting finisher).  Writes t to tsm[0].
+__device__ __forceinline__ unsigned long long finish_topk_hist(
+    const uint2* L, int c, int k, int n, float Mx, float lo, float u, float* Bb, uint32_t* hist,
+    uint32_t* Bi, float* tsm, unsigned char* masks, float* probs) {
+  const int lane = (int)lane_id();
+  float t = Mx;
+  if (k > 1) {
+    hist[lane] = 0u;
+    hist[lane + 32] = 0u;
+    const float d = __fsub_rn(Mx, lo);
+    const float scale = d > 0.0f ? __fmul_rn(64.0f, __frcp_rn(d)) : 0.0f;
+    __syncwarp();
+    for (int j = lane; j < c; j += 32) atomicAdd(&hist[kbucket(ex(L[j]), lo, scale)], 1u);
+    __syncwarp();
+    // Suffix counts from the top bucket down: suf = candidates in buckets
+    // >= 2 * lane.
+    const uint32_t h0 = hist[2 * lane], h1 = hist[2 * lane + 1];
+    uint32_t suf = h0 + h1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t w = __shfl_down_sync(FULL, suf, o);
+      if (lane + o < 32) suf += w;
+    }
+    // Highest lane whose suffix reaches k (lane 0 holds c >= k).
+    const unsigned ball = __ballot_sync(FULL, suf >= (uint32_t)k);
+    const int Lh = 31 - __clz(ball);
+    const uint32_t sL = __shfl_sync(FULL, suf, Lh);
+    const uint32_t a0 = __shfl_sync(FULL, h0, Lh), a1 = __shfl_sync(FULL, h1, Lh);
+    int B;
+    uint32_t above, nB;
+    if (sL - a0 >= (uint32_t)k) {
+      B = 2 * Lh + 1;
+      above = sL - a0 - a1;
+      nB = a1;
+    } else {
+      B = 2 * Lh;
+      above = sL - a0;
+      nB = a0;
+    }
+    if (nB > 32u) return pack_out(Q3S_STATUS_NOT_RUN, 0u);
+    const uint32_t need = (uint32_t)k - above;  // 1 <= need <= nB
+    // Gather bucket B's values, rank them exactly.
+    float* G = reinterpret_cast<float*>(Bi);
+    uint32_t base = 0;
+    for (int j0 = 0; j0 < c; j0 += 32) {
+      const int j = j0 + lane;
+      float x = 0.0f;
+      bool in = false;
+      if (j < c) {
+        x = ex(L[j]);
+        in = kbucket(x, lo, scale) == B;
+      }
+      const unsigned bb = __ballot_sync(FULL, in);
+      if (in) G[base + __popc(bb & lanemask_lt())] = x;
+      base += __popc(bb);
+    }
+    __syncwarp();
+    const float g = lane < (int)nB ? G[lane] : 0.0f;
+    uint32_t gt = 0, ge = 0;
+    for (int i = 0; i < (int)nB; ++i) {
+      const float w = __shfl_sync(FULL, g, i);
+      gt += w > g ? 1u : 0u;
+      ge += w >= g ? 1u : 0u;
+    }
+    const unsigned hit = __ballot_sync(FULL, lane < (int)nB && gt < need && need <= ge);
+    t = __shfl_sync(FULL, g, __ffs(hit) - 1);
+    __syncwarp();
+  }
+  if (lane == 0) tsm[0] = t;
+  // Survivors in vocabulary order with their softmax numerators.
+  int ns = 0;
+  for (int j0 = 0; j0 < c; j0 += 32) {
+    const int j = j0 + lane;
+    uint2 en = make_uint2(0u, 0u);
+    bool sv = false;
+    if (j < c) {
+      en = L[j];
+      sv = ex(en) >= t;
+    }
+    const unsigned bb = __ballot_sync(FULL, sv);
+    if (sv) {
+      const int d = ns + __popc(bb & lanemask_lt());
+      Bb[d] = cr_expf(__fsub_rn(ex(en), Mx));
+      Bi[d] = en.y;
+    }
+    ns += __popc(bb);
+  }
+  if (lane < ((4 - (ns & 3)) & 3)) Bb[ns + lane] = 0.0f;  // zero-pad to a multiple of 4 (<= ROW_CAP)
+  __syncwarp();
+  const float sum = chain_prefix(Bb, ns);
+  if (!is_finite(sum) || sum <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
+  const float thr = __fmul_rn(u, sum);
+  uint32_t token = (uint32_t)(n - 1);
+  for (int j0 = 0; j0 < ns; j0 += 32) {
+    const int j = j0 + lane;
+    const unsigned bb = __ballot_sync(FULL, j < ns && Bb[j] >= thr);
+    if (bb) {
+      token = Bi[j0 + __ffs(bb) - 1];
+      break;
+    }
+  }
+  if (masks || probs) {
+    for (int j = lane; j < c; j += 32) {
+      const float x = ex(L[j]);
+      if (x >= t) {
+        if (masks) masks[L[j].y] |= 4;
+        if (probs)
+          probs[L[j].y] = __double2float_rn((double)cr_expf(__fsub_rn(x, Mx)) / (double)sum);
+      }
+    }
+  }
+  __syncwarp();
+  return pack_out(Q3S_STATUS_OK, token);
+}
+
 // Debug pass over the stage: bit0 finite x, bit1 x >= t (OR-ed in).
 template <int DT, bool XF>
 __device__ void debug_masks(const FastSpace& f, const RowCtx& r, float t, unsigned char* masks) {
@@ -1037,8 +1259,8 @@ __device__ bool fast_row(const FastSpace& f, const StageView& s, const RowMeta& 
   }
   const int k = (int)P.top_k;
   const int hi = k <= 128 ? max(2 * k, 64) : k + 96;
-  float tau;
-  if (!find_tau(vm, mx, k, hi, delta, tau)) return false;
+  float tau = mx;  // k == 1: the maximum and its ties
+  if (k > 1 && !find_tau(vm, mx, k, hi, delta, tau)) return false;
   // Raw-domain selection: lower tau until its image lies strictly below the
   // image of tau, so no element below the new tau can tie the k-th largest
   // x after the multiply.
@@ -1054,29 +1276,31 @@ __device__ bool fast_row(const FastSpace& f, const StageView& s, const RowMeta& 
     if (!ok) return false;
     tau = t2;
   }
-  uint64_t flags = 0;
-#pragma unroll
-  for (int j = 0; j < NJ; ++j) flags |= (vm[j] >= tau ? 1ull : 0ull) << j;
-  const int mine = count_cands<DT, XF, EDGE>(f, rc, flags, tau);
-  const int incl = (int)warp_inclusive_scan((uint32_t)mine);
-  const int c = __shfl_sync(FULL, incl, 31);
-  if (c < k || c > ROW_CAP) return false;
-  write_cands<DT, XF, EDGE>(f, rc, flags, tau, f.list + (incl - mine));
-  __syncwarp();
+  const uint32_t flags = chunk_flags(vm, tau);
+  const int c = collect_cands<DT, NJ, XF, EDGE>(f, rc, flags, tau,
+                                                reinterpret_cast<uint16_t*>(f.Kb), f.list);
+  if (c < k) return false;  // more than ROW_CAP candidates (or none: impossible)
   if (!dbg.masks) release<DT>(rel);
   const int use_top_p = P.top_p < 1.0 ? 1 : 0;
   const float top_p = (float)P.top_p;
   float* tsm = reinterpret_cast<float*>(f.hist);
-  unsigned long long r;
-  if (c <= 32)
-    r = finish_warp<1>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, f.Bb, f.Kb, tsm, dbg.masks,
-                       dbg.probs);
-  else if (c <= 128)
-    r = finish_warp<4>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, f.Bb, f.Kb, tsm, dbg.masks,
-                       dbg.probs);
-  else
-    r = finish_warp<16>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, f.Bb, f.Kb, tsm, dbg.masks,
-                        dbg.probs);
+  unsigned long long r = pack_out(Q3S_STATUS_NOT_RUN, 0u);
+  if (!use_top_p) {
+    const float lo = XF ? tau : __fmul_rn(tau, rc.inv);
+    r = finish_topk_hist(f.list, c, k, s.n, Mx, lo, u, f.Bb, f.hist + 64,
+                         reinterpret_cast<uint32_t*>(f.Kb), tsm, dbg.masks, dbg.probs);
+  }
+  if ((int)(r >> 32) == Q3S_STATUS_NOT_RUN) {
+    if (c <= 32)
+      r = finish_warp<1>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, f.Bb, f.Kb, tsm, dbg.masks,
+                         dbg.probs);
+    else if (c <= 128)
+      r = finish_warp<4>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, f.Bb, f.Kb, tsm, dbg.masks,
+                         dbg.probs);
+    else
+      r = finish_warp<16>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, f.Bb, f.Kb, tsm, dbg.masks,
+                          dbg.probs);
+  }
   out = {(int)(r >> 32), (uint32_t)r};
   if (dbg.masks) {
     __syncwarp();
@@ -1129,10 +1353,10 @@ __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const Gen
   const float u = a.uniform_override ? m.uo : philox_uniform(m.seed, m.subseq, P.ctr_lo);
   const bool inv_ok = rc.inv > 0.0f && rc.inv < __int_as_float(0x7f800000);
   const bool fast = inv_ok && P.top_k >= 1u && P.top_k <= (uint32_t)FAST_MAX_K &&
-                    P.top_k < (uint32_t)s.n;
+                    P.top_k < (uint32_t)s.n && s.Q <= 32 * NJ;
   if (fast) {
     const bool xf = rc.use_pen || rc.sf >= 0;
-    const bool edge = s.mis != 0 || (s.n % Elem<DT>::EPV) != 0;
+    const bool edge = s.mis != 0 || (s.n % Elem<DT>::EPV) != 0 || s.Q != 32 * NJ;
     RowOut out;
     bool done;
     if (xf)
@@ -1306,18 +1530,17 @@ int sample_max_warps(int vcap, int dtype, size_t smem_limit) {
 }
 
 cudaError_t launch_sample(const KernelArgs& a, int grid, int warps, cudaStream_t stream) {
-  // NJ: 16-byte vectors per lane for the largest row (plus one for a
-  // misaligned start).
+  // NJ: the lane chunk of the fast-path scan for the row capacity.
   if (a.dtype == Q3S_DTYPE_F32) {
-    const int q = (a.vcap * 4 + 15) / 16 + 1;
-    if (q <= 32 * 8) return launch_t<Q3S_DTYPE_F32, 8>(a, grid, warps, stream);
-    if (q <= 32 * 17) return launch_t<Q3S_DTYPE_F32, 17>(a, grid, warps, stream);
-    if (q <= 32 * 25) return launch_t<Q3S_DTYPE_F32, 25>(a, grid, warps, stream);
-    return launch_t<Q3S_DTYPE_F32, 33>(a, grid, warps, stream);
+    switch (chunk_vectors(a.vcap, 4)) {
+      case 8: return launch_t<Q3S_DTYPE_F32, 8>(a, grid, warps, stream);
+      case 16: return launch_t<Q3S_DTYPE_F32, 16>(a, grid, warps, stream);
+      case 24: return launch_t<Q3S_DTYPE_F32, 24>(a, grid, warps, stream);
+      default: return launch_t<Q3S_DTYPE_F32, 32>(a, grid, warps, stream);
+    }
   }
-  const int q = (a.vcap * 2 + 15) / 16 + 1;
-  if (q <= 32 * 9) return launch_t<Q3S_DTYPE_BF16, 9>(a, grid, warps, stream);
-  return launch_t<Q3S_DTYPE_BF16, 17>(a, grid, warps, stream);
+  if (chunk_vectors(a.vcap, 2) == 8) return launch_t<Q3S_DTYPE_BF16, 8>(a, grid, warps, stream);
+  return launch_t<Q3S_DTYPE_BF16, 16>(a, grid, warps, stream);
 }
 
 cudaError_t launch_greedy(const void* logits, int dtype, long long num_rows, long long row_stride,
