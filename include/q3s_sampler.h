@@ -152,8 +152,8 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* batch, void* stream);
  * keeps no device workspace.  Same arguments and results as
  * q3s_sample_batch; in addition it rejects vocab > Q3S_MAX_VOCAB with
  * Q3S_E_INVALID_ARGUMENT, and it launches only as many blocks as the array
- * holds workspace for (about 14 bytes per vocabulary entry per warp, 8 warps
- * a block: 146 blocks at vocab 2048, 97 at 3072, 73 at 4096).  The first call on
+ * holds workspace for (about 14 bytes per vocabulary entry per warp, up to 12 warps
+ * a block: 97 blocks at vocab 2048, 65 at 3072 and 4096).  The first call on
  * a device looks up the array's address (cudaGetSymbolAddress, which may load
  * the module): make it before any stream capture.  Calls share the array and
  * nothing in it has to start at zero; calls whose kernels overlap on the GPU

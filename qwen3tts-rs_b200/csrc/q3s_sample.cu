@@ -47,7 +47,7 @@
 namespace q3s {
 namespace {
 
-constexpr int MAX_WARPS = 8;
+constexpr int MAX_WARPS = 12;
 constexpr int ROW_CAP = 512;      // candidates one fast row may hold
 constexpr int FAST_MAX_K = 256;
 constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;  // bounded wait for a stage: 1 s
@@ -79,20 +79,26 @@ __host__ __device__ inline size_t stage_bytes(int vcap, int es) {
   return row > chunks ? row : chunks;
 }
 
-// Per-warp shared memory.
+// Per-warp shared memory (19.2 KB for a 3072-entry f32 row, so 12 warps fit
+// an SM).  Kb is one 2 KB area whose users never overlap in time: the
+// flagged-vector list of the collection, the k-th-value gather and softmax
+// terms of the top-k finisher, the sort keys (aliasing the softmax terms) of
+// the top-p finisher, and the general path's sort keys.
+constexpr int KB_BYTES = 2048;
+constexpr int HIST_WORDS = 80;  // [0]: top-k threshold t; [16, 80): k-th-value histogram
+
 struct FastSpace {
   unsigned char* stage;     // raw row, TMA destination
-  uint2* list;              // [ROW_CAP] candidates (x bits, index)
-  float* Bb;                // [ROW_CAP] softmax terms, then running sums
-  unsigned long long* Kb;   // [ROW_CAP] sorted nucleus keys; general-path sort space
+  uint2* list;              // [ROW_CAP] candidates (x bits, index); general-path histogram
+  unsigned long long* Kb;   // KB_BYTES, see above
   uint32_t* bm;             // [vcap/32] history bitmap
-  uint32_t* hist;           // [256]
+  uint32_t* hist;           // [HIST_WORDS]
   uint64_t* mbar;           // stage barrier
 };
 
 __host__ __device__ inline size_t fast_bytes(int vcap, int es) {
-  return stage_bytes(vcap, es) + 8u * ROW_CAP + 4u * ROW_CAP + 8u * ROW_CAP +
-         align16(4u * (vcap / 32)) + 4u * 256 + 16u;
+  return stage_bytes(vcap, es) + 8u * ROW_CAP + KB_BYTES + 4u * HIST_WORDS +
+         align16(4u * (vcap / 32)) + 16u;
 }
 
 __device__ inline FastSpace carve_fast(unsigned char* base, int vcap, int es) {
@@ -102,14 +108,12 @@ __device__ inline FastSpace carve_fast(unsigned char* base, int vcap, int es) {
   o += stage_bytes(vcap, es);
   f.list = reinterpret_cast<uint2*>(base + o);
   o += 8u * ROW_CAP;
-  f.Bb = reinterpret_cast<float*>(base + o);
-  o += 4u * ROW_CAP;
   f.Kb = reinterpret_cast<unsigned long long*>(base + o);
-  o += 8u * ROW_CAP;
+  o += KB_BYTES;
+  f.hist = reinterpret_cast<uint32_t*>(base + o);
+  o += 4u * HIST_WORDS;
   f.bm = reinterpret_cast<uint32_t*>(base + o);
   o += align16(4u * (vcap / 32));
-  f.hist = reinterpret_cast<uint32_t*>(base + o);
-  o += 4u * 256;
   f.mbar = reinterpret_cast<uint64_t*>(base + o);
   return f;
 }
@@ -773,14 +777,18 @@ __device__ __forceinline__ int count_ge(const float (&vm)[NJ], float tau) {
   return (int)__reduce_add_sync(FULL, (unsigned)c);
 }
 
-// A distance d below the row maximum such that between k and hi vectors have
-// their maximum at or above mx - d.  Starts from the warp's previous distance;
-// false when no finite threshold reaches k vectors.
+// A threshold tau such that between k and hi vectors have their maximum at
+// or above it, searched as a distance d below the row maximum.  The first
+// probe is the warp's previous threshold `prev` (an absolute value: it
+// tracks rows of similar distribution far better than a distance from a row
+// maximum that fluctuates), nudged toward the middle of the window after
+// each acceptance.  False when no finite threshold reaches k vectors.
 template <int NJ>
-__device__ bool find_tau(const float (&vm)[NJ], float mx, int k, int hi, float& delta,
+__device__ bool find_tau(const float (&vm)[NJ], float mx, int k, int hi, float& prev,
                          float& tau) {
   float lo = 0.0f, dhi = -1.0f, best = -1.0f;
-  float d = delta > 0.0f ? delta : 1.0f;
+  float d = __fsub_rn(mx, prev);
+  if (!(d > 0.0f && d < __int_as_float(0x7f800000))) d = 1.0f;  // no (usable) previous
 #pragma unroll 1
   for (int it = 0; it < 48; ++it) {
     const float t = __fsub_rn(mx, d);
@@ -789,14 +797,12 @@ __device__ bool find_tau(const float (&vm)[NJ], float mx, int k, int hi, float& 
     if (c >= k) best = best < 0.0f ? d : fminf(best, d);
     if (c < k) {
       lo = d;
-      d = dhi < 0.0f ? __fmul_rn(d, 4.0f) : 0.5f * (lo + dhi);
+      d = dhi < 0.0f ? __fmul_rn(d, 2.0f) : 0.5f * (lo + dhi);
     } else if (c > hi) {
       dhi = d;
       d = 0.5f * (lo + dhi);
     } else {
-      // Accepted: the next row starts from d nudged toward the middle of
-      // the window.
-      delta = 2 * c < k + hi ? __fmul_rn(d, 1.03125f) : __fmul_rn(d, 0.96875f);
+      prev = __fsub_rn(mx, 2 * c < k + hi ? __fmul_rn(d, 1.03125f) : __fmul_rn(d, 0.96875f));
       tau = t;
       return true;
     }
@@ -804,8 +810,8 @@ __device__ bool find_tau(const float (&vm)[NJ], float mx, int k, int hi, float& 
     if (!(d < __int_as_float(0x7f800000))) break;
   }
   if (best < 0.0f) return false;
-  delta = best;
   tau = __fsub_rn(mx, best);
+  prev = tau;
   return tau > neg_inf();
 }
 
@@ -1057,6 +1063,12 @@ __device__ __noinline__ unsigned long long finish_warp(const uint2* L, int c, in
   return pack_out(Q3S_STATUS_OK, token);
 }
 
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(FULL, v, o));
+  return v;
+}
+
 // Bucket of x in [lo, lo + 64/scale) for the k-th-value histogram: a
 // monotone map of x (equal values share a bucket), clamped to [0, 63].
 __device__ __forceinline__ int kbucket(float x, float lo, float scale) {
@@ -1094,88 +1106,116 @@ __device__ __forceinline__ float chain_prefix(float* B, int count) {
 }
 
 // Finishes a row without top-p from its candidates L[0..c) in vocabulary
-// order (x after the temperature, index), k <= c: the statements of
-// sampling.rs:654-663 and 700-729 on the candidate set, which holds every
+// order (x after the temperature, index), k <= c <= ROW_CAP: the statements
+// of sampling.rs:654-663 and 700-729 on the candidate set, which holds every
 // element >= the k-th largest x (all others are masked by top-k).
 //   * t, the k-th largest x (ties kept): a 64-bucket histogram of the
-//     candidates over [lo, Mx] locates the bucket holding the k-th largest;
-//     the few values in that bucket are ranked exactly.
-//   * The survivors x >= t, still in vocabulary order, get exp(x - Mx)
-//     (masked entries are exact zeros of the reference's sums and are
-//     skipped); one lane accumulates the sequential f32 prefix sums, and the
-//     draw is the first survivor whose running sum reaches u * sum.
-// Returns pack_out(status, token); returns pack_out(NOT_RUN, 0) when the
-// bucket of the k-th value holds more than 32 candidates (the caller then
-// uses the sorting finisher).  Writes t to tsm[0].
+//     candidates in a value interval [a, b] (first [lo, Mx]) locates the
+//     bucket holding the k-th largest.  A bucket of at most 32 values is
+//     ranked exactly; a fuller one becomes the next interval (its own
+//     minimum and maximum, which land in different buckets, so every level
+//     shrinks it).  The bucket map is monotone, so a bucket's members are
+//     exactly the candidates between its minimum and maximum.
+//   * The survivors x >= t are compacted in place, still in vocabulary
+//     order, with exp(x - Mx) in Bb (masked entries are exact zeros of the
+//     reference's sums and are skipped); one lane accumulates the sequential
+//     f32 prefix sums, and the draw is the first survivor whose running sum
+//     reaches u * sum.
+// Bb: >= ROW_CAP floats (also the gather space).  Writes t to tsm[0].
 __device__ __forceinline__ unsigned long long finish_topk_hist(
-    const uint2* L, int c, int k, int n, float Mx, float lo, float u, float* Bb, uint32_t* hist,
-    uint32_t* Bi, float* tsm, unsigned char* masks, float* probs) {
+    uint2* L, int c, int k, int n, float Mx, float lo, float u, float* Bb, uint32_t* hist,
+    float* tsm, unsigned char* masks, float* probs) {
   const int lane = (int)lane_id();
+  const uint32_t lt = lanemask_lt();
   float t = Mx;
   if (k > 1) {
-    hist[lane] = 0u;
-    hist[lane + 32] = 0u;
-    const float d = __fsub_rn(Mx, lo);
-    const float scale = d > 0.0f ? __fmul_rn(64.0f, __frcp_rn(d)) : 0.0f;
-    __syncwarp();
-    for (int j = lane; j < c; j += 32) atomicAdd(&hist[kbucket(ex(L[j]), lo, scale)], 1u);
-    __syncwarp();
-    // Suffix counts from the top bucket down: suf = candidates in buckets
-    // >= 2 * lane.
-    const uint32_t h0 = hist[2 * lane], h1 = hist[2 * lane + 1];
-    uint32_t suf = h0 + h1;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t w = __shfl_down_sync(FULL, suf, o);
-      if (lane + o < 32) suf += w;
-    }
-    // Highest lane whose suffix reaches k (lane 0 holds c >= k).
-    const unsigned ball = __ballot_sync(FULL, suf >= (uint32_t)k);
-    const int Lh = 31 - __clz(ball);
-    const uint32_t sL = __shfl_sync(FULL, suf, Lh);
-    const uint32_t a0 = __shfl_sync(FULL, h0, Lh), a1 = __shfl_sync(FULL, h1, Lh);
-    int B;
-    uint32_t above, nB;
-    if (sL - a0 >= (uint32_t)k) {
-      B = 2 * Lh + 1;
-      above = sL - a0 - a1;
-      nB = a1;
-    } else {
-      B = 2 * Lh;
-      above = sL - a0;
-      nB = a0;
-    }
-    if (nB > 32u) return pack_out(Q3S_STATUS_NOT_RUN, 0u);
-    const uint32_t need = (uint32_t)k - above;  // 1 <= need <= nB
-    // Gather bucket B's values, rank them exactly.
-    float* G = reinterpret_cast<float*>(Bi);
-    uint32_t base = 0;
-    for (int j0 = 0; j0 < c; j0 += 32) {
-      const int j = j0 + lane;
-      float x = 0.0f;
-      bool in = false;
-      if (j < c) {
-        x = ex(L[j]);
-        in = kbucket(x, lo, scale) == B;
+    float a = lo, b = Mx;
+    uint32_t need = (uint32_t)k;  // rank of t among the candidates in [a, b], from the top
+#pragma unroll 1
+    while (true) {
+      if (!(a < b)) {
+        t = b;
+        break;
       }
-      const unsigned bb = __ballot_sync(FULL, in);
-      if (in) G[base + __popc(bb & lanemask_lt())] = x;
-      base += __popc(bb);
+      const float d = __fsub_rn(b, a);
+      const float scale = __fmul_rn(64.0f, __frcp_rn(d < __int_as_float(0x7f800000) ? d : 3.40282347e38f));
+      hist[lane] = 0u;
+      hist[lane + 32] = 0u;
+      __syncwarp();
+      for (int j = lane; j < c; j += 32) {
+        const float x = ex(L[j]);
+        if (a <= x && x <= b) atomicAdd(&hist[kbucket(x, a, scale)], 1u);
+      }
+      __syncwarp();
+      // Suffix counts from the top bucket down: suf = members in buckets
+      // >= 2 * lane (lane 0: all members, >= need).
+      const uint32_t h0 = hist[2 * lane], h1 = hist[2 * lane + 1];
+      uint32_t suf = h0 + h1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t w = __shfl_down_sync(FULL, suf, o);
+        if (lane + o < 32) suf += w;
+      }
+      const unsigned ball = __ballot_sync(FULL, suf >= need);
+      const int Lh = 31 - __clz(ball);
+      const uint32_t sL = __shfl_sync(FULL, suf, Lh);
+      const uint32_t a0 = __shfl_sync(FULL, h0, Lh), a1 = __shfl_sync(FULL, h1, Lh);
+      int B;
+      uint32_t nB;
+      if (sL - a0 >= need) {
+        B = 2 * Lh + 1;
+        need -= sL - a0 - a1;
+        nB = a1;
+      } else {
+        B = 2 * Lh;
+        need -= sL - a0;
+        nB = a0;
+      }
+      // 1 <= need <= nB.
+      if (nB <= 32u) {
+        // Gather bucket B and rank its values exactly.
+        uint32_t base = 0;
+        for (int j0 = 0; j0 < c; j0 += 32) {
+          const int j = j0 + lane;
+          float x = 0.0f;
+          bool in = false;
+          if (j < c) {
+            x = ex(L[j]);
+            in = a <= x && x <= b && kbucket(x, a, scale) == B;
+          }
+          const unsigned bb = __ballot_sync(FULL, in);
+          if (in) Bb[base + __popc(bb & lt)] = x;
+          base += __popc(bb);
+        }
+        __syncwarp();
+        const float g = lane < (int)nB ? Bb[lane] : 0.0f;
+        uint32_t gt = 0, ge = 0;
+        for (int i = 0; i < (int)nB; ++i) {
+          const float w = __shfl_sync(FULL, g, i);
+          gt += w > g ? 1u : 0u;
+          ge += w >= g ? 1u : 0u;
+        }
+        const unsigned hit = __ballot_sync(FULL, lane < (int)nB && gt < need && need <= ge);
+        t = __shfl_sync(FULL, g, __ffs(hit) - 1);
+        __syncwarp();
+        break;
+      }
+      // Next interval: bucket B's own extent.
+      float mn = __int_as_float(0x7f800000), mxb = neg_inf();
+      for (int j = lane; j < c; j += 32) {
+        const float x = ex(L[j]);
+        if (a <= x && x <= b && kbucket(x, a, scale) == B) {
+          mn = fminf(mn, x);
+          mxb = fmaxf(mxb, x);
+        }
+      }
+      a = warp_min(mn);
+      b = warp_max(mxb);
     }
-    __syncwarp();
-    const float g = lane < (int)nB ? G[lane] : 0.0f;
-    uint32_t gt = 0, ge = 0;
-    for (int i = 0; i < (int)nB; ++i) {
-      const float w = __shfl_sync(FULL, g, i);
-      gt += w > g ? 1u : 0u;
-      ge += w >= g ? 1u : 0u;
-    }
-    const unsigned hit = __ballot_sync(FULL, lane < (int)nB && gt < need && need <= ge);
-    t = __shfl_sync(FULL, g, __ffs(hit) - 1);
-    __syncwarp();
   }
   if (lane == 0) tsm[0] = t;
-  // Survivors in vocabulary order with their softmax numerators.
+  // Survivors, compacted in place (d <= j, and every read of an iteration
+  // precedes its writes), with their softmax numerators.
   int ns = 0;
   for (int j0 = 0; j0 < c; j0 += 32) {
     const int j = j0 + lane;
@@ -1187,9 +1227,9 @@ __device__ __forceinline__ unsigned long long finish_topk_hist(
     }
     const unsigned bb = __ballot_sync(FULL, sv);
     if (sv) {
-      const int d = ns + __popc(bb & lanemask_lt());
+      const int d = ns + __popc(bb & lt);
+      L[d] = en;
       Bb[d] = cr_expf(__fsub_rn(ex(en), Mx));
-      Bi[d] = en.y;
     }
     ns += __popc(bb);
   }
@@ -1203,18 +1243,16 @@ __device__ __forceinline__ unsigned long long finish_topk_hist(
     const int j = j0 + lane;
     const unsigned bb = __ballot_sync(FULL, j < ns && Bb[j] >= thr);
     if (bb) {
-      token = Bi[j0 + __ffs(bb) - 1];
+      token = L[j0 + __ffs(bb) - 1].y;
       break;
     }
   }
   if (masks || probs) {
-    for (int j = lane; j < c; j += 32) {
-      const float x = ex(L[j]);
-      if (x >= t) {
-        if (masks) masks[L[j].y] |= 4;
-        if (probs)
-          probs[L[j].y] = __double2float_rn((double)cr_expf(__fsub_rn(x, Mx)) / (double)sum);
-      }
+    for (int j = lane; j < ns; j += 32) {
+      const uint2 en = L[j];
+      if (masks) masks[en.y] |= 4;
+      if (probs)
+        probs[en.y] = __double2float_rn((double)cr_expf(__fsub_rn(ex(en), Mx)) / (double)sum);
     }
   }
   __syncwarp();
@@ -1280,26 +1318,26 @@ __device__ bool fast_row(const FastSpace& f, const StageView& s, const RowMeta& 
   const int c = collect_cands<DT, NJ, XF, EDGE>(f, rc, flags, tau,
                                                 reinterpret_cast<uint16_t*>(f.Kb), f.list);
   if (c < k) return false;  // more than ROW_CAP candidates (or none: impossible)
-  if (!dbg.masks) release<DT>(rel);
   const int use_top_p = P.top_p < 1.0 ? 1 : 0;
+  if (use_top_p && c > 256) return false;  // the sorting finisher holds 256 keys
+  if (!dbg.masks) release<DT>(rel);
   const float top_p = (float)P.top_p;
   float* tsm = reinterpret_cast<float*>(f.hist);
-  unsigned long long r = pack_out(Q3S_STATUS_NOT_RUN, 0u);
+  float* Bb = reinterpret_cast<float*>(f.Kb);
+  unsigned long long r;
   if (!use_top_p) {
     const float lo = XF ? tau : __fmul_rn(tau, rc.inv);
-    r = finish_topk_hist(f.list, c, k, s.n, Mx, lo, u, f.Bb, f.hist + 64,
-                         reinterpret_cast<uint32_t*>(f.Kb), tsm, dbg.masks, dbg.probs);
-  }
-  if ((int)(r >> 32) == Q3S_STATUS_NOT_RUN) {
-    if (c <= 32)
-      r = finish_warp<1>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, f.Bb, f.Kb, tsm, dbg.masks,
+    r = finish_topk_hist(f.list, c, k, s.n, Mx, lo, u, Bb, f.hist + 16, tsm, dbg.masks,
                          dbg.probs);
-    else if (c <= 128)
-      r = finish_warp<4>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, f.Bb, f.Kb, tsm, dbg.masks,
-                         dbg.probs);
-    else
-      r = finish_warp<16>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, f.Bb, f.Kb, tsm, dbg.masks,
-                          dbg.probs);
+  } else if (c <= 32) {
+    r = finish_warp<1>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, Bb, f.Kb, tsm, dbg.masks,
+                       dbg.probs);
+  } else if (c <= 128) {
+    r = finish_warp<4>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, Bb, f.Kb, tsm, dbg.masks,
+                       dbg.probs);
+  } else {
+    r = finish_warp<8>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, Bb, f.Kb, tsm, dbg.masks,
+                       dbg.probs);
   }
   out = {(int)(r >> 32), (uint32_t)r};
   if (dbg.masks) {
@@ -1372,7 +1410,7 @@ __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const Gen
   __syncwarp();
   release<DT>(rel);
   const unsigned long long r = general_compute(
-      g.A, g.B, g.BX, g.BI, f.bm, f.hist, f.Kb, s.n,
+      g.A, g.B, g.BX, g.BI, f.bm, reinterpret_cast<uint32_t*>(f.list), f.Kb, s.n,
       rc.inv, rc.pf, rc.use_pen ? 1 : 0, rc.sf, rc.allow, P.top_k, P.top_p, u, dbg.masks,
       dbg.probs);
   return {(int)(r >> 32), (uint32_t)r};
@@ -1398,7 +1436,7 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
   long long row = gw;
   if (row < a.num_rows && lane == 0) issue_row<DT>(a, row, f);
   uint32_t phase = 0;
-  float delta = 0.0f;
+  float delta = __int_as_float(0x7fc00000);  // previous tau of this warp (none yet)
   // Per-row metadata is loaded one row ahead so its latency overlaps a row.
   RowMeta cur;
   if (row < a.num_rows) cur = load_meta(a, row);
