@@ -47,7 +47,8 @@
 namespace q3s {
 namespace {
 
-constexpr int MAX_WARPS = 12;
+constexpr int MAX_WARPS = 16;
+constexpr int RING = 8;  // row stages per block, shared by its warps
 constexpr int ROW_CAP = 512;      // candidates one fast row may hold
 constexpr int FAST_MAX_K = 256;
 constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;  // bounded wait for a stage: 1 s
@@ -79,33 +80,51 @@ __host__ __device__ inline size_t stage_bytes(int vcap, int es) {
   return row > chunks ? row : chunks;
 }
 
-// Per-warp shared memory (19.2 KB for a 3072-entry f32 row, so 12 warps fit
-// an SM).  Kb is one 2 KB area whose users never overlap in time: the
-// flagged-vector list of the collection, the k-th-value gather and softmax
-// terms of the top-k finisher, the sort keys (aliasing the softmax terms) of
-// the top-p finisher, and the general path's sort keys.
+// Per-warp shared memory (6.8 KB for a 3072-entry row; with the 8 shared
+// row stages, 16 warps fit an SM).  Kb is one 2 KB area whose users never
+// overlap in time: the flagged-vector list of the collection, the
+// k-th-value gather and softmax terms of the top-k finisher, the sort keys
+// (aliasing the softmax terms) of the top-p finisher, and the general
+// path's sort keys.
 constexpr int KB_BYTES = 2048;
 constexpr int HIST_WORDS = 80;  // [0]: top-k threshold t; [16, 80): k-th-value histogram
 
 struct FastSpace {
-  unsigned char* stage;     // raw row, TMA destination
+  unsigned char* stage;     // the current row's ring stage (TMA destination)
   uint2* list;              // [ROW_CAP] candidates (x bits, index); general-path histogram
   unsigned long long* Kb;   // KB_BYTES, see above
   uint32_t* bm;             // [vcap/32] history bitmap
   uint32_t* hist;           // [HIST_WORDS]
-  uint64_t* mbar;           // stage barrier
 };
 
-__host__ __device__ inline size_t fast_bytes(int vcap, int es) {
-  return stage_bytes(vcap, es) + 8u * ROW_CAP + KB_BYTES + 4u * HIST_WORDS +
-         align16(4u * (vcap / 32)) + 16u;
+// Shared memory of a block: the ring control block, RING stages, then one
+// area per warp.  Rows go to warps by ticket (in order); ticket t uses stage
+// t % RING, generation t / RING.  A stage's generation g+1 is issued by the
+// warp of generation g once it has read the stage, and `issued` lets a warp
+// wait for its own generation before testing the barrier's phase parity
+// (parity alone cannot tell generation g+1 from g-1).
+struct RingCtl {
+  uint64_t full[RING];      // stage barriers (one arrival + the copy's bytes)
+  uint32_t issued[RING];    // generations issued per stage
+  uint32_t consumed[RING];  // generations waited for per stage
+  uint32_t ticket;          // next ticket
+  uint32_t abort;           // set when a wait gave up: no more copies, rows NOT_RUN
+};
+constexpr size_t CTL_BYTES = 256;
+static_assert(sizeof(RingCtl) <= CTL_BYTES, "ring control block");
+
+__host__ __device__ inline size_t warp_bytes(int vcap) {
+  return 8u * ROW_CAP + KB_BYTES + 4u * HIST_WORDS + align16(4u * (vcap / 32));
 }
 
-__device__ inline FastSpace carve_fast(unsigned char* base, int vcap, int es) {
+__host__ __device__ inline size_t block_smem(int vcap, int es, int warps) {
+  return CTL_BYTES + RING * stage_bytes(vcap, es) + (size_t)warps * warp_bytes(vcap);
+}
+
+__device__ inline FastSpace carve_warp(unsigned char* base, int vcap) {
   FastSpace f;
   size_t o = 0;
-  f.stage = base;
-  o += stage_bytes(vcap, es);
+  f.stage = nullptr;
   f.list = reinterpret_cast<uint2*>(base + o);
   o += 8u * ROW_CAP;
   f.Kb = reinterpret_cast<unsigned long long*>(base + o);
@@ -113,8 +132,6 @@ __device__ inline FastSpace carve_fast(unsigned char* base, int vcap, int es) {
   f.hist = reinterpret_cast<uint32_t*>(base + o);
   o += 4u * HIST_WORDS;
   f.bm = reinterpret_cast<uint32_t*>(base + o);
-  o += align16(4u * (vcap / 32));
-  f.mbar = reinterpret_cast<uint64_t*>(base + o);
   return f;
 }
 
@@ -149,6 +166,8 @@ struct StageView {
   int n;    // elements
   int mis;  // leading misalignment in elements
   int Q;    // 16-byte vectors covering the row
+  const void* p0;     // the row in global memory (element 0)
+  const uint4* g16;   // global 16-byte vector q of the stage layout is g16[q]
 };
 
 // Row geometry shared by the copy issuer and the consumer.
@@ -190,7 +209,7 @@ __device__ __forceinline__ bool row_fits(const KernelArgs& a, int n) {
 // Lane 0: arms the stage barrier and starts the interior bulk copy of `row`.
 // Rows that do not fit the stage arm the barrier with no bytes.
 template <int DT>
-__device__ void issue_row(const KernelArgs& a, long long row, const FastSpace& f) {
+__device__ void issue_row(const KernelArgs& a, long long row, unsigned char* stage, uint64_t* bar) {
   constexpr int es = Elem<DT>::BYTES;
   const int n = row_vocab(a, row);
   uint32_t bytes = 0;
@@ -199,13 +218,13 @@ __device__ void issue_row(const KernelArgs& a, long long row, const FastSpace& f
     g = row_geom(a, row, n, es);
     bytes = g.tail_begin - g.head_end;
   }
-  mbar_arrive_expect_tx(f.mbar, bytes);
-  if (bytes > 0) bulk_copy_g2s(f.stage + g.mis_bytes + g.head_end, g.p0 + g.head_end, bytes, f.mbar);
+  mbar_arrive_expect_tx(bar, bytes);
+  if (bytes > 0) bulk_copy_g2s(stage + g.mis_bytes + g.head_end, g.p0 + g.head_end, bytes, bar);
 }
 
 // After the barrier completes: the lanes copy the unaligned head and tail.
 template <int DT>
-__device__ StageView complete_stage(const KernelArgs& a, long long row, int n, const FastSpace& f) {
+__device__ StageView complete_stage(const KernelArgs& a, long long row, int n, unsigned char* stage) {
   constexpr int es = Elem<DT>::BYTES;
   const RowGeom g = row_geom(a, row, n, es);
   const unsigned lane = lane_id();
@@ -213,16 +232,16 @@ __device__ StageView complete_stage(const KernelArgs& a, long long row, int n, c
   const int t0 = (int)(g.tail_begin / es);
   for (int i = lane; i < hn; i += 32) {
     if (es == 4)
-      reinterpret_cast<float*>(f.stage + g.mis_bytes)[i] = __ldg(reinterpret_cast<const float*>(g.p0) + i);
+      reinterpret_cast<float*>(stage + g.mis_bytes)[i] = __ldg(reinterpret_cast<const float*>(g.p0) + i);
     else
-      reinterpret_cast<unsigned short*>(f.stage + g.mis_bytes)[i] =
+      reinterpret_cast<unsigned short*>(stage + g.mis_bytes)[i] =
           __ldg(reinterpret_cast<const unsigned short*>(g.p0) + i);
   }
   for (int i = t0 + lane; i < n; i += 32) {
     if (es == 4)
-      reinterpret_cast<float*>(f.stage + g.mis_bytes)[i] = __ldg(reinterpret_cast<const float*>(g.p0) + i);
+      reinterpret_cast<float*>(stage + g.mis_bytes)[i] = __ldg(reinterpret_cast<const float*>(g.p0) + i);
     else
-      reinterpret_cast<unsigned short*>(f.stage + g.mis_bytes)[i] =
+      reinterpret_cast<unsigned short*>(stage + g.mis_bytes)[i] =
           __ldg(reinterpret_cast<const unsigned short*>(g.p0) + i);
   }
   __syncwarp();
@@ -230,6 +249,8 @@ __device__ StageView complete_stage(const KernelArgs& a, long long row, int n, c
   v.n = n;
   v.mis = (int)(g.mis_bytes / es);
   v.Q = (int)((g.mis_bytes + g.bytes + 15u) / 16u);
+  v.p0 = g.p0;
+  v.g16 = reinterpret_cast<const uint4*>(g.p0 - g.mis_bytes);
   return v;
 }
 
@@ -253,12 +274,6 @@ __device__ __forceinline__ void unpack_vec(const uint4& v, float (&e)[Elem<DT>::
 template <int DT>
 __device__ __forceinline__ void unpack(const unsigned char* stage, int q, float (&e)[Elem<DT>::EPV]) {
   unpack_vec<DT>(*reinterpret_cast<const uint4*>(stage + 16 * q), e);
-}
-
-template <int DT>
-__device__ __forceinline__ float stage_elem(const unsigned char* stage, int mis, int i) {
-  if (DT == Q3S_DTYPE_F32) return reinterpret_cast<const float*>(stage)[mis + i];
-  return __uint_as_float(((uint32_t) reinterpret_cast<const unsigned short*>(stage)[mis + i]) << 16);
 }
 
 // Everything the kernel reads about a row besides its logits.
@@ -302,6 +317,7 @@ __device__ __forceinline__ bool idx_allowed(int i, int sf, int allow) {
 // Per-row transform inputs.
 struct RowCtx {
   int n, mis, Q;
+  const uint4* g16;  // the row's 16-byte vectors in global memory (stage layout)
   float inv;      // 1 / (temperature as f32)
   float pf;       // repetition penalty as f32
   bool use_pen;
@@ -595,6 +611,7 @@ __device__ __noinline__ unsigned long long general_compute(
   rc.n = n;
   rc.mis = 0;
   rc.Q = 0;
+  rc.g16 = nullptr;
   rc.inv = inv;
   rc.pf = pf;
   rc.use_pen = use_pen != 0;
@@ -705,11 +722,16 @@ __device__ __noinline__ unsigned long long general_compute(
 // Fast path: warp scan and candidate collection.
 // ===========================================================================
 
-// The stage is released (to the next row's copy) exactly once per row.
+// A row's stage is released exactly once, as soon as the row no longer
+// reads it: lane 0 issues the stage's next generation (ticket + RING) and
+// publishes it in `issued`.
 struct Releaser {
   const KernelArgs* a;
-  const FastSpace* f;
-  long long next;
+  RingCtl* ctl;
+  unsigned char* stage;
+  int slot;
+  long long next;  // row of the stage's next generation
+  uint32_t gen;    // that generation
   bool done;
 };
 
@@ -718,10 +740,31 @@ __device__ __forceinline__ void release(Releaser& r) {
   if (r.done) return;
   r.done = true;
   __syncwarp();
-  if (lane_id() == 0) {
+  if (lane_id() == 0 && r.next < r.a->num_rows &&
+      *reinterpret_cast<volatile uint32_t*>(&r.ctl->abort) == 0u) {
     fence_proxy_async_smem();
-    if (r.next < r.a->num_rows) issue_row<DT>(*r.a, r.next, *r.f);
+    issue_row<DT>(*r.a, r.next, r.stage, &r.ctl->full[r.slot]);
+    __threadfence_block();
+    *reinterpret_cast<volatile uint32_t*>(&r.ctl->issued[r.slot]) = r.gen + 1u;
   }
+}
+
+// Waits for generation `gen` of stage `slot`: first until it has been issued
+// (a later generation's parity must not be tested against an earlier
+// phase), then for its bytes.  False when a wait gave up or the block aborts.
+__device__ bool wait_stage(RingCtl* ctl, int slot, uint32_t gen) {
+  if (*reinterpret_cast<volatile uint32_t*>(&ctl->abort) != 0u) return false;
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (*reinterpret_cast<volatile uint32_t*>(&ctl->issued[slot]) <= gen) {
+    if (*reinterpret_cast<volatile uint32_t*>(&ctl->abort) != 0u) return false;
+    __nanosleep(128);
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > WAIT_LIMIT_NS) return false;
+  }
+  __threadfence_block();
+  return mbar_wait_bounded(&ctl->full[slot], gen & 1u, WAIT_LIMIT_NS);
 }
 
 // Vector maxima of the stage (registers) and the row maximum.  Lane l owns
@@ -848,7 +891,7 @@ __device__ __forceinline__ int collect_cands(const FastSpace& f, const RowCtx& r
     if (i < NF) {
       q = Qs[i];
       float e[EPV];
-      unpack<DT>(f.stage, q, e);
+      unpack_vec<DT>(__ldg(r.g16 + q), e);
 #pragma unroll
       for (int c = 0; c < EPV; ++c) {
         x[c] = xform<XF, EDGE>(e[c], q * EPV + c - r.mis, r);
@@ -1261,10 +1304,10 @@ __device__ __forceinline__ unsigned long long finish_topk_hist(
 
 // Debug pass over the stage: bit0 finite x, bit1 x >= t (OR-ed in).
 template <int DT, bool XF>
-__device__ void debug_masks(const FastSpace& f, const RowCtx& r, float t, unsigned char* masks) {
+__device__ void debug_masks(const void* p0, const RowCtx& r, float t, unsigned char* masks) {
   const unsigned lane = lane_id();
   for (int i = lane; i < r.n; i += 32) {
-    float x = xform<XF, false>(stage_elem<DT>(f.stage, r.mis, i), i, r);
+    float x = xform<XF, false>(load_elem<DT>(p0, i), i, r);
     if (!XF) x = is_finite(x) ? __fmul_rn(x, r.inv) : neg_inf();
     unsigned char m = 0;
     if (is_finite(x)) m = 1;
@@ -1274,8 +1317,8 @@ __device__ void debug_masks(const FastSpace& f, const RowCtx& r, float t, unsign
   __syncwarp();
 }
 
-// Fast path.  Returns false (before releasing the stage) when the row must
-// take the general path instead.
+// Fast path.  Returns false when the row must take the general path
+// instead (which reads the row from global memory).
 template <int DT, int NJ, bool XF, bool EDGE>
 __device__ bool fast_row(const FastSpace& f, const StageView& s, const RowMeta& m,
                          const RowCtx& rc, float u, Releaser& rel, float& delta, RowOut& out,
@@ -1283,6 +1326,7 @@ __device__ bool fast_row(const FastSpace& f, const StageView& s, const RowMeta& 
   const q3s_row_params& P = m.P;
   float vm[NJ];
   const float mx = scan_stage<DT, NJ, XF, EDGE>(f, rc, vm);
+  release<DT>(rel);  // everything below reads the row from global memory
   if (!XF && mx == __int_as_float(0x7f800000)) return false;  // raw +inf
   if (mx == neg_inf() || mx != mx) {
     release<DT>(rel);
@@ -1320,7 +1364,6 @@ __device__ bool fast_row(const FastSpace& f, const StageView& s, const RowMeta& 
   if (c < k) return false;  // more than ROW_CAP candidates (or none: impossible)
   const int use_top_p = P.top_p < 1.0 ? 1 : 0;
   if (use_top_p && c > 256) return false;  // the sorting finisher holds 256 keys
-  if (!dbg.masks) release<DT>(rel);
   const float top_p = (float)P.top_p;
   float* tsm = reinterpret_cast<float*>(f.hist);
   float* Bb = reinterpret_cast<float*>(f.Kb);
@@ -1342,8 +1385,7 @@ __device__ bool fast_row(const FastSpace& f, const StageView& s, const RowMeta& 
   out = {(int)(r >> 32), (uint32_t)r};
   if (dbg.masks) {
     __syncwarp();
-    debug_masks<DT, XF>(f, rc, tsm[0], dbg.masks);
-    release<DT>(rel);
+    debug_masks<DT, XF>(s.p0, rc, tsm[0], dbg.masks);
   }
   return true;
 }
@@ -1382,6 +1424,7 @@ __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const Gen
   rc.n = s.n;
   rc.mis = s.mis;
   rc.Q = s.Q;
+  rc.g16 = s.g16;
   rc.inv = __fdiv_rn(1.0f, (float)P.temperature);
   rc.pf = (float)P.repetition_penalty;
   rc.sf = P.suppress_from;
@@ -1406,9 +1449,9 @@ __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const Gen
     if (done) return out;
   }
   const unsigned lane = lane_id();
-  for (int i = lane; i < s.n; i += 32) g.A[i] = stage_elem<DT>(f.stage, s.mis, i);
-  __syncwarp();
   release<DT>(rel);
+  for (int i = lane; i < s.n; i += 32) g.A[i] = load_elem<DT>(s.p0, i);
+  __syncwarp();
   const unsigned long long r = general_compute(
       g.A, g.B, g.BX, g.BI, f.bm, reinterpret_cast<uint32_t*>(f.list), f.Kb, s.n,
       rc.inv, rc.pf, rc.use_pen ? 1 : 0, rc.sf, rc.allow, P.top_k, P.top_p, u, dbg.masks,
@@ -1423,27 +1466,45 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
   const int warp = threadIdx.x >> 5;
   const int warps = blockDim.x >> 5;
   const unsigned lane = lane_id();
-  const FastSpace f = carve_fast(smem + (size_t)warp * fast_bytes(a.vcap, es), a.vcap, es);
+  RingCtl* ctl = reinterpret_cast<RingCtl*>(smem);
+  const size_t sbytes = stage_bytes(a.vcap, es);
+  unsigned char* ring = smem + CTL_BYTES;
+  FastSpace f = carve_warp(ring + RING * sbytes + (size_t)warp * warp_bytes(a.vcap), a.vcap);
   const long long gw = (long long)blockIdx.x * warps + warp;
   const GenSpace g = carve_gen(a.scratch + (size_t)gw * gen_bytes(a.vcap), a.vcap);
-  if (lane == 0) {
-    mbar_init(f.mbar, 1);
+  const long long G = gridDim.x;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < RING; ++s) {
+      mbar_init(&ctl->full[s], 1);
+      ctl->issued[s] = 0u;
+      ctl->consumed[s] = 0u;
+    }
+    ctl->ticket = 0u;
+    ctl->abort = 0u;
     fence_mbarrier_init();
     fence_proxy_async_smem();
+    for (int s = 0; s < RING; ++s) {
+      const long long row = blockIdx.x + (long long)s * G;
+      if (row < a.num_rows) {
+        issue_row<DT>(a, row, ring + s * sbytes, &ctl->full[s]);
+        ctl->issued[s] = 1u;
+      }
+    }
   }
-  __syncwarp();
-  const long long stride = (long long)gridDim.x * warps;
-  long long row = gw;
-  if (row < a.num_rows && lane == 0) issue_row<DT>(a, row, f);
-  uint32_t phase = 0;
+  __syncthreads();
   float delta = __int_as_float(0x7fc00000);  // previous tau of this warp (none yet)
-  // Per-row metadata is loaded one row ahead so its latency overlaps a row.
-  RowMeta cur;
-  if (row < a.num_rows) cur = load_meta(a, row);
-  for (; row < a.num_rows; row += stride) {
-    Releaser rel{&a, &f, row + stride, false};
-    RowMeta nxt;
-    if (row + stride < a.num_rows) nxt = load_meta(a, row + stride);
+#pragma unroll 1
+  while (true) {
+    uint32_t t = 0;
+    if (lane == 0) t = atomicAdd(&ctl->ticket, 1u);
+    t = __shfl_sync(FULL, t, 0);
+    const long long row = blockIdx.x + (long long)t * G;
+    if (row >= a.num_rows) break;
+    const int slot = (int)(t % RING);
+    const uint32_t gen = t / RING;
+    f.stage = ring + slot * sbytes;
+    Releaser rel{&a, ctl, f.stage, slot, blockIdx.x + (long long)(t + RING) * G, gen + 1u, false};
+    const RowMeta cur = load_meta(a, row);
     const int n = cur.n;
     const q3s_row_params& P = cur.P;
     int st = row_fits(a, n) ? validate(P) : Q3S_STATUS_UNSUPPORTED;
@@ -1455,7 +1516,7 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
     if (dbg.probs)
       for (int i = lane; i < n; i += 32) dbg.probs[i] = 0.0f;
     // History bitmap of a sampled row with a penalty (filled while the
-    // stage copy is in flight).
+    // stage copy may still be in flight).
     if (st == Q3S_STATUS_OK && P.do_sample && P.repetition_penalty != 1.0 && cur.h1 > cur.h0) {
       const int words = (n + 31) >> 5;
       for (int w = lane; w < words; w += 32) f.bm[w] = 0u;
@@ -1466,22 +1527,22 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
       }
       __syncwarp();
     }
-    const bool ready = mbar_wait_bounded(f.mbar, phase, WAIT_LIMIT_NS);
-    phase ^= 1u;
-    if (!ready) {
-      // The stage never arrived: mark this warp's remaining rows and stop
-      // after another bounded wait for the copy in flight.
-      mbar_wait_bounded(f.mbar, phase ^ 1u, WAIT_LIMIT_NS);
-      for (long long r = row; r < a.num_rows; r += stride)
-        if (lane == 0) {
-          a.tokens[r] = 0u;
-          a.status[r] = (unsigned char)Q3S_STATUS_NOT_RUN;
-        }
-      return;
+    const bool ready = wait_stage(ctl, slot, gen);
+    if (!__all_sync(FULL, ready)) {
+      // A wait gave up (or the block aborts): this row is not run, no copy
+      // is issued any more, and later tickets fail fast.
+      if (lane == 0) {
+        atomicExch(&ctl->abort, 1u);
+        a.tokens[row] = 0u;
+        a.status[row] = (unsigned char)Q3S_STATUS_NOT_RUN;
+      }
+      __syncwarp();
+      continue;
     }
+    if (lane == 0) ctl->consumed[slot] = gen + 1u;
     RowOut out{st, 0u};
     if (st == Q3S_STATUS_OK) {
-      const StageView s = complete_stage<DT>(a, row, n, f);
+      const StageView s = complete_stage<DT>(a, row, n, f.stage);
       if (!P.do_sample) {
         out = greedy_stage<DT>(f, s, P.suppress_from, P.allow_token);
       } else {
@@ -1494,8 +1555,14 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
       a.status[row] = (unsigned char)out.status;
     }
     __syncwarp();
-    cur = nxt;
   }
+  // After an abort, copies may still be in flight into the ring: wait (with
+  // a limit) for each before the block's shared memory goes away.
+  __syncthreads();
+  if (threadIdx.x == 0 && ctl->abort != 0u)
+    for (int s = 0; s < RING; ++s)
+      if (ctl->issued[s] > ctl->consumed[s])
+        mbar_wait_bounded(&ctl->full[s], ctl->consumed[s] & 1u, WAIT_LIMIT_NS);
 }
 
 // Greedy argmax rows (sampling.rs:40-60 and :72-117), one warp per row.
@@ -1545,7 +1612,7 @@ __global__ void greedy_kernel(const void* logits, long long num_rows, long long 
 
 template <int DT, int NJ>
 cudaError_t launch_t(const KernelArgs& a, int grid, int warps, cudaStream_t stream) {
-  const size_t smem = fast_bytes(a.vcap, Elem<DT>::BYTES) * (size_t)warps;
+  const size_t smem = block_smem(a.vcap, Elem<DT>::BYTES, warps);
   cudaError_t e = cudaFuncSetAttribute(sample_kernel<DT, NJ>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -1556,14 +1623,16 @@ cudaError_t launch_t(const KernelArgs& a, int grid, int warps, cudaStream_t stre
 }  // namespace
 
 size_t sample_smem_per_warp(int vcap, int dtype) {
-  return fast_bytes(vcap, dtype == Q3S_DTYPE_F32 ? 4 : 2);
+  (void)dtype;
+  return warp_bytes(vcap);
 }
 
 size_t sample_scratch_per_warp(int vcap) { return gen_bytes(vcap); }
 
 int sample_max_warps(int vcap, int dtype, size_t smem_limit) {
-  const size_t per = sample_smem_per_warp(vcap, dtype);
-  int w = (int)(smem_limit / per);
+  const size_t fixed = block_smem(vcap, dtype == Q3S_DTYPE_F32 ? 4 : 2, 0);
+  if (smem_limit <= fixed) return 0;
+  int w = (int)((smem_limit - fixed) / warp_bytes(vcap));
   return w > MAX_WARPS ? MAX_WARPS : w;
 }
 
