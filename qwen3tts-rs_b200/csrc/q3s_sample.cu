@@ -86,8 +86,10 @@ __host__ __device__ inline size_t stage_bytes(int vcap, int es) {
 // k-th-value gather and softmax terms of the top-k finisher, the sort keys
 // (aliasing the softmax terms) of the top-p finisher, and the general
 // path's sort keys.
-constexpr int KB_BYTES = 2048;
-constexpr int HIST_WORDS = 80;  // [0]: top-k threshold t; [16, 80): k-th-value histogram
+constexpr int KB_BYTES = 2048 + 32;  // 512 softmax terms + zero padding to a multiple of 8
+// [0]: top-k threshold t; [16, 80): k-th-value bucket counts; [80, 144) and
+// [144, 208): the largest and smallest order key per bucket.
+constexpr int HIST_WORDS = 208;
 
 struct FastSpace {
   unsigned char* stage;     // the current row's ring stage (TMA destination)
@@ -858,15 +860,50 @@ __device__ bool find_tau(const float (&vm)[NJ], float mx, int k, int hi, float& 
   return tau > neg_inf();
 }
 
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(FULL, v, o));
+  return v;
+}
+
+// Bucket of x in [lo, lo + 64/scale) for the k-th-value histogram: a
+// monotone map of x (equal values share a bucket), clamped to [0, 63].
+__device__ __forceinline__ int kbucket(float x, float lo, float scale) {
+  const float y = __fmul_rn(__fsub_rn(x, lo), scale);
+  // NaN (0 * inf) and y <= 0 go to bucket 0; truncation of y in (0, 63) is
+  // its floor.
+  return y > 0.0f ? (y >= 63.0f ? 63 : (int)y) : 0;
+}
+
+// Zeroes a level of the k-th-value histogram (counts, largest and smallest
+// order key per bucket).
+__device__ __forceinline__ void hist_clear(uint32_t* h) {
+  const int lane = (int)lane_id();
+  h[lane] = 0u;
+  h[lane + 32] = 0u;
+  h[64 + lane] = 0u;
+  h[96 + lane] = 0u;
+  h[128 + lane] = 0xFFFFFFFFu;
+  h[160 + lane] = 0xFFFFFFFFu;
+}
+
+__device__ __forceinline__ void hist_add(uint32_t* h, int b, float x) {
+  const uint32_t key = total_key(x);
+  atomicAdd(&h[b], 1u);
+  atomicMax(&h[64 + b], key);
+  atomicMin(&h[128 + b], key);
+}
+
 // The candidates {x >= tau} of the flagged vectors, in vocabulary order, as
 // (x after the temperature, index) into L.  The flagged vectors are first
-// listed warp-wide (lane-major = vocabulary order) in Qs, then processed 32
+// listed warp-wide (lane-major = vocabulary order) in Qs, then read back
+// from global memory (L2: the row was staged moments ago) and processed 32
 // at a time, one per lane, with ballot prefix counts placing each lane's
 // candidates.  Returns the number of candidates, or -1 when there are more
 // than ROW_CAP.
 template <int DT, int NJ, bool XF, bool EDGE>
-__device__ __forceinline__ int collect_cands(const FastSpace& f, const RowCtx& r, uint32_t flags,
-                                             float tau, uint16_t* Qs, uint2* L) {
+__device__ __forceinline__ int collect_cands(const RowCtx& r, uint32_t flags, float tau,
+                                             uint16_t* Qs, uint2* L) {
   constexpr int EPV = Elem<DT>::EPV;
   const int lane = (int)lane_id();
   const int nf = __popc(flags);
@@ -885,11 +922,10 @@ __device__ __forceinline__ int collect_cands(const FastSpace& f, const RowCtx& r
   int base = 0;
   for (int i0 = 0; i0 < NF; i0 += 32) {
     const int i = i0 + lane;
+    const int q = i < NF ? (int)Qs[i] : -1;
     float x[EPV];
     uint32_t bits = 0;
-    int q = 0;
-    if (i < NF) {
-      q = Qs[i];
+    if (q >= 0) {
       float e[EPV];
       unpack_vec<DT>(__ldg(r.g16 + q), e);
 #pragma unroll
@@ -899,7 +935,6 @@ __device__ __forceinline__ int collect_cands(const FastSpace& f, const RowCtx& r
       }
     }
     const int cnt = __popc(bits);
-    // Exclusive prefix of cnt (0..EPV) over the lanes from its binary digits.
     int pre = 0, tot = 0;
 #pragma unroll
     for (int d = 0; (1 << d) <= EPV; ++d) {
@@ -1106,42 +1141,70 @@ __device__ __noinline__ unsigned long long finish_warp(const uint2* L, int c, in
   return pack_out(Q3S_STATUS_OK, token);
 }
 
-__device__ __forceinline__ float warp_min(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(FULL, v, o));
-  return v;
-}
-
-// Bucket of x in [lo, lo + 64/scale) for the k-th-value histogram: a
-// monotone map of x (equal values share a bucket), clamped to [0, 63].
-__device__ __forceinline__ int kbucket(float x, float lo, float scale) {
-  const float y = __fmul_rn(__fsub_rn(x, lo), scale);
-  // NaN (0 * inf) and y <= 0 go to bucket 0; truncation of y in (0, 63) is
-  // its floor.
-  return y > 0.0f ? (y >= 63.0f ? 63 : (int)y) : 0;
+// exp(x) for x <= 0 (finite or -inf): cr_expf without the NaN and overflow
+// branches, which such arguments never take; same operations otherwise.
+__device__ __forceinline__ float cr_expf_nonpos(float xf) {
+  if (xf < -104.0f) return 0.0f;
+  const double x = (double)xf;
+  const double kd = rint(__dmul_rn(x, 0x1.71547652b82fep+0));
+  double r = __fma_rn(-kd, 0x1.62e42fefa39efp-1, x);
+  r = __fma_rn(-kd, 0x1.abc9e3b39803fp-56, r);
+  double p = 0x1.6124613a86d09p-33;
+  p = __fma_rn(p, r, 0x1.1eed8eff8d898p-29);
+  p = __fma_rn(p, r, 0x1.ae64567f544e4p-26);
+  p = __fma_rn(p, r, 0x1.27e4fb7789f5cp-22);
+  p = __fma_rn(p, r, 0x1.71de3a556c734p-19);
+  p = __fma_rn(p, r, 0x1.a01a01a01a01ap-16);
+  p = __fma_rn(p, r, 0x1.a01a01a01a01ap-13);
+  p = __fma_rn(p, r, 0x1.6c16c16c16c17p-10);
+  p = __fma_rn(p, r, 0x1.1111111111111p-7);
+  p = __fma_rn(p, r, 0x1.5555555555555p-5);
+  p = __fma_rn(p, r, 0x1.5555555555555p-3);
+  p = __fma_rn(p, r, 0.5);
+  p = __fma_rn(p, r, 1.0);
+  p = __fma_rn(p, r, 1.0);
+  const long long k = (long long)kd;
+  const double scale = __longlong_as_double((k + 1023LL) << 52);
+  return __double2float_rn(__dmul_rn(p, scale));
 }
 
 // Sequential f32 prefix sums of B[0..count) in place by lane 0 (B 16-byte
-// aligned and zero-padded to a multiple of 4); returns the total to every
-// lane.  Loads run one vector ahead of the additions.
+// aligned and zero-padded to a multiple of 8); returns the total to every
+// lane.  Eight terms per step, loads one step ahead of the additions.
 __device__ __forceinline__ float chain_prefix(float* B, int count) {
   float c = 0.0f;
   if (lane_id() == 0) {
     float4* B4 = reinterpret_cast<float4*>(B);
-    const int n4 = (count + 3) >> 2;
-    float4 nx = n4 > 0 ? B4[0] : make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int q = 0; q < n4; ++q) {
-      float4 v = nx;
-      if (q + 1 < n4) nx = B4[q + 1];
-      c = __fadd_rn(c, v.x);
-      v.x = c;
-      c = __fadd_rn(c, v.y);
-      v.y = c;
-      c = __fadd_rn(c, v.z);
-      v.z = c;
-      c = __fadd_rn(c, v.w);
-      v.w = c;
-      B4[q] = v;
+    const int n8 = (count + 7) >> 3;
+    float4 na = make_float4(0.f, 0.f, 0.f, 0.f), nb = na;
+    if (n8 > 0) {
+      na = B4[0];
+      nb = B4[1];
+    }
+    for (int q = 0; q < n8; ++q) {
+      float4 va = na, vb = nb;
+      if (q + 1 < n8) {
+        na = B4[2 * q + 2];
+        nb = B4[2 * q + 3];
+      }
+      c = __fadd_rn(c, va.x);
+      va.x = c;
+      c = __fadd_rn(c, va.y);
+      va.y = c;
+      c = __fadd_rn(c, va.z);
+      va.z = c;
+      c = __fadd_rn(c, va.w);
+      va.w = c;
+      c = __fadd_rn(c, vb.x);
+      vb.x = c;
+      c = __fadd_rn(c, vb.y);
+      vb.y = c;
+      c = __fadd_rn(c, vb.z);
+      vb.z = c;
+      c = __fadd_rn(c, vb.w);
+      vb.w = c;
+      B4[2 * q] = va;
+      B4[2 * q + 1] = vb;
     }
   }
   __syncwarp();
@@ -1152,21 +1215,24 @@ __device__ __forceinline__ float chain_prefix(float* B, int count) {
 // order (x after the temperature, index), k <= c <= ROW_CAP: the statements
 // of sampling.rs:654-663 and 700-729 on the candidate set, which holds every
 // element >= the k-th largest x (all others are masked by top-k).
-//   * t, the k-th largest x (ties kept): a 64-bucket histogram of the
-//     candidates in a value interval [a, b] (first [lo, Mx]) locates the
-//     bucket holding the k-th largest.  A bucket of at most 32 values is
-//     ranked exactly; a fuller one becomes the next interval (its own
-//     minimum and maximum, which land in different buckets, so every level
-//     shrinks it).  The bucket map is monotone, so a bucket's members are
-//     exactly the candidates between its minimum and maximum.
+//   * t, the k-th largest x (ties kept): a 64-bucket histogram (count,
+//     largest and smallest order key per bucket) of the candidates in a
+//     value interval [a, b] (first [lo, Mx]) locates the bucket holding the
+//     k-th largest.  When t is the bucket's largest or smallest value it is
+//     read off directly; a bucket of at most 32 values is ranked exactly; a
+//     fuller one becomes the next interval (its own smallest and largest
+//     value, which land in different buckets, so every level shrinks it).
+//     The bucket map is monotone, so a bucket's members are exactly the
+//     candidates between its smallest and largest value.
 //   * The survivors x >= t are compacted in place, still in vocabulary
 //     order, with exp(x - Mx) in Bb (masked entries are exact zeros of the
 //     reference's sums and are skipped); one lane accumulates the sequential
 //     f32 prefix sums, and the draw is the first survivor whose running sum
 //     reaches u * sum.
-// Bb: >= ROW_CAP floats (also the gather space).  Writes t to tsm[0].
+// h: the histogram (HIST_WORDS - 16 words); Bb: ROW_CAP + 8 floats (also the
+// gather space).  Writes t to tsm[0].
 __device__ __forceinline__ unsigned long long finish_topk_hist(
-    uint2* L, int c, int k, int n, float Mx, float lo, float u, float* Bb, uint32_t* hist,
+    uint2* L, int c, int k, int n, float Mx, float lo, float u, float* Bb, uint32_t* h,
     float* tsm, unsigned char* masks, float* probs) {
   const int lane = (int)lane_id();
   const uint32_t lt = lanemask_lt();
@@ -1181,18 +1247,18 @@ __device__ __forceinline__ unsigned long long finish_topk_hist(
         break;
       }
       const float d = __fsub_rn(b, a);
-      const float scale = __fmul_rn(64.0f, __frcp_rn(d < __int_as_float(0x7f800000) ? d : 3.40282347e38f));
-      hist[lane] = 0u;
-      hist[lane + 32] = 0u;
+      const float scale =
+          __fmul_rn(64.0f, __frcp_rn(d < __int_as_float(0x7f800000) ? d : 3.40282347e38f));
+      hist_clear(h);
       __syncwarp();
       for (int j = lane; j < c; j += 32) {
         const float x = ex(L[j]);
-        if (a <= x && x <= b) atomicAdd(&hist[kbucket(x, a, scale)], 1u);
+        if (a <= x && x <= b) hist_add(h, kbucket(x, a, scale), x);
       }
       __syncwarp();
       // Suffix counts from the top bucket down: suf = members in buckets
       // >= 2 * lane (lane 0: all members, >= need).
-      const uint32_t h0 = hist[2 * lane], h1 = hist[2 * lane + 1];
+      const uint32_t h0 = h[2 * lane], h1 = h[2 * lane + 1];
       uint32_t suf = h0 + h1;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -1215,6 +1281,14 @@ __device__ __forceinline__ unsigned long long finish_topk_hist(
         nB = a0;
       }
       // 1 <= need <= nB.
+      if (need == 1u) {
+        t = from_total_key(h[64 + B]);
+        break;
+      }
+      if (need == nB) {
+        t = from_total_key(h[128 + B]);
+        break;
+      }
       if (nB <= 32u) {
         // Gather bucket B and rank its values exactly.
         uint32_t base = 0;
@@ -1244,16 +1318,9 @@ __device__ __forceinline__ unsigned long long finish_topk_hist(
         break;
       }
       // Next interval: bucket B's own extent.
-      float mn = __int_as_float(0x7f800000), mxb = neg_inf();
-      for (int j = lane; j < c; j += 32) {
-        const float x = ex(L[j]);
-        if (a <= x && x <= b && kbucket(x, a, scale) == B) {
-          mn = fminf(mn, x);
-          mxb = fmaxf(mxb, x);
-        }
-      }
-      a = warp_min(mn);
-      b = warp_max(mxb);
+      a = from_total_key(h[128 + B]);
+      b = from_total_key(h[64 + B]);
+      __syncwarp();
     }
   }
   if (lane == 0) tsm[0] = t;
@@ -1272,11 +1339,11 @@ __device__ __forceinline__ unsigned long long finish_topk_hist(
     if (sv) {
       const int d = ns + __popc(bb & lt);
       L[d] = en;
-      Bb[d] = cr_expf(__fsub_rn(ex(en), Mx));
+      Bb[d] = cr_expf_nonpos(__fsub_rn(ex(en), Mx));
     }
     ns += __popc(bb);
   }
-  if (lane < ((4 - (ns & 3)) & 3)) Bb[ns + lane] = 0.0f;  // zero-pad to a multiple of 4 (<= ROW_CAP)
+  if (lane < ((8 - (ns & 7)) & 7)) Bb[ns + lane] = 0.0f;  // zero-pad to a multiple of 8
   __syncwarp();
   const float sum = chain_prefix(Bb, ns);
   if (!is_finite(sum) || sum <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
@@ -1359,16 +1426,17 @@ __device__ bool fast_row(const FastSpace& f, const StageView& s, const RowMeta& 
     tau = t2;
   }
   const uint32_t flags = chunk_flags(vm, tau);
-  const int c = collect_cands<DT, NJ, XF, EDGE>(f, rc, flags, tau,
+  const int use_top_p = P.top_p < 1.0 ? 1 : 0;
+  const int c = collect_cands<DT, NJ, XF, EDGE>(rc, flags, tau,
                                                 reinterpret_cast<uint16_t*>(f.Kb), f.list);
   if (c < k) return false;  // more than ROW_CAP candidates (or none: impossible)
-  const int use_top_p = P.top_p < 1.0 ? 1 : 0;
   if (use_top_p && c > 256) return false;  // the sorting finisher holds 256 keys
   const float top_p = (float)P.top_p;
   float* tsm = reinterpret_cast<float*>(f.hist);
   float* Bb = reinterpret_cast<float*>(f.Kb);
   unsigned long long r;
   if (!use_top_p) {
+    // Every candidate lies in [lo, Mx].
     const float lo = XF ? tau : __fmul_rn(tau, rc.inv);
     r = finish_topk_hist(f.list, c, k, s.n, Mx, lo, u, Bb, f.hist + 16, tsm, dbg.masks,
                          dbg.probs);
