@@ -114,13 +114,15 @@ struct RingCtl {
 };
 constexpr size_t CTL_BYTES = 256;
 static_assert(sizeof(RingCtl) <= CTL_BYTES, "ring control block");
+// The plan ring (PLAN_SLOTS x 32 bytes) follows the control block.
+constexpr size_t HEAD_BYTES = CTL_BYTES + 96 * 32;
 
 __host__ __device__ inline size_t warp_bytes(int vcap) {
   return 8u * ROW_CAP + KB_BYTES + 4u * HIST_WORDS + align16(4u * (vcap / 32));
 }
 
 __host__ __device__ inline size_t block_smem(int vcap, int es, int warps) {
-  return CTL_BYTES + RING * stage_bytes(vcap, es) + (size_t)warps * warp_bytes(vcap);
+  return HEAD_BYTES + RING * stage_bytes(vcap, es) + (size_t)warps * warp_bytes(vcap);
 }
 
 __device__ inline FastSpace carve_warp(unsigned char* base, int vcap) {
@@ -278,30 +280,6 @@ __device__ __forceinline__ void unpack(const unsigned char* stage, int q, float 
   unpack_vec<DT>(*reinterpret_cast<const uint4*>(stage + 16 * q), e);
 }
 
-// Everything the kernel reads about a row besides its logits.
-struct RowMeta {
-  q3s_row_params P;
-  int n;
-  long long h0, h1;  // history range
-  unsigned long long seed, subseq;
-  float uo;  // uniform override
-};
-
-__device__ __forceinline__ RowMeta load_meta(const KernelArgs& a, long long row) {
-  RowMeta m;
-  m.n = row_vocab(a, row);
-  m.P = a.params[row * a.params_stride];
-  m.h0 = m.h1 = 0;
-  if (a.history_offsets) {
-    m.h0 = a.history_offsets[row];
-    m.h1 = a.history_offsets[row + 1];
-  }
-  m.seed = a.seeds ? a.seeds[row] : 0ull;
-  m.subseq = a.subseqs ? a.subseqs[row] : 0ull;
-  m.uo = a.uniform_override ? a.uniform_override[row] : 0.0f;
-  return m;
-}
-
 // Option validation of sampling.rs:281-296 (f64 comparisons).
 __device__ inline int validate(const q3s_row_params& p) {
   if (!isfinite(p.repetition_penalty) || p.repetition_penalty <= 0.0)
@@ -314,6 +292,91 @@ __device__ inline int validate(const q3s_row_params& p) {
 
 __device__ __forceinline__ bool idx_allowed(int i, int sf, int allow) {
   return sf < 0 || i < sf || (allow >= 0 && i == allow);
+}
+
+// A row's parameters as the kernel uses them (32 bytes), computed ahead for
+// 32 rows at a time, one lane per row: the draw, the f32 casts, the
+// validation status and the flags.  suppress_from / allow_token are clamped
+// to [-1, n], which keeps every comparison with an index below n.
+struct RowPlan {
+  float u;       // the draw: Philox word 0 of (seed, subseq, ctr_lo), or the override
+  float inv;     // 1 / (temperature as f32)
+  float pf;      // repetition penalty as f32
+  float top_p;   // top_p as f32
+  uint32_t k;    // top_k
+  uint32_t nf;   // row vocabulary (low 16 bits) | flags (high 16 bits)
+  uint32_t sa;   // suppress_from (low 16, signed) | allow_token (high 16, signed)
+  uint32_t tag;  // the ticket this plan belongs to
+};
+static_assert(sizeof(RowPlan) == 32, "plan record");
+constexpr uint32_t PF_STATUS = 7u;  // Q3S_STATUS_* of the row (validation, vocabulary)
+constexpr uint32_t PF_DO_SAMPLE = 1u << 3;
+constexpr uint32_t PF_USE_PEN = 1u << 4;  // sampled, penalty != 1 and a non-empty history
+constexpr uint32_t PF_TOP_P = 1u << 5;    // top_p < 1
+constexpr uint32_t NO_TAG = 0xFFFFFFFFu;
+constexpr int PLAN_SLOTS = 96;  // three batches of 32 tickets
+
+__device__ __forceinline__ uint32_t clamp16(long long v, int n) {
+  const int c = v < 0 ? -1 : (v > n ? n : (int)v);
+  return (uint32_t)(uint16_t)(int16_t)c;
+}
+
+__device__ RowPlan compute_plan(const KernelArgs& a, long long row, uint32_t ticket) {
+  const q3s_row_params P = a.params[row * a.params_stride];
+  int n = row_vocab(a, row);
+  const int st = row_fits(a, n) ? validate(P) : Q3S_STATUS_UNSUPPORTED;
+  n = n < 0 ? 0 : (n > 65535 ? 65535 : n);
+  uint32_t flags = (uint32_t)st;
+  if (P.do_sample) flags |= PF_DO_SAMPLE;
+  if (P.top_p < 1.0) flags |= PF_TOP_P;
+  if (P.do_sample && P.repetition_penalty != 1.0 && a.history_offsets &&
+      a.history_offsets[row + 1] > a.history_offsets[row])
+    flags |= PF_USE_PEN;
+  RowPlan p;
+  p.u = a.uniform_override ? a.uniform_override[row]
+                           : philox_uniform(a.seeds[row], a.subseqs[row], P.ctr_lo);
+  p.inv = __fdiv_rn(1.0f, (float)P.temperature);
+  p.pf = (float)P.repetition_penalty;
+  p.top_p = (float)P.top_p;
+  p.k = P.top_k;
+  p.nf = (uint32_t)n | (flags << 16);
+  p.sa = clamp16(P.suppress_from, n) | (clamp16(P.allow_token, n) << 16);
+  p.tag = ticket;
+  return p;
+}
+
+// Publishes a plan: the tag is invalidated first and written last, so a
+// reader that sees the same matching tag before and after reading the data
+// read a consistent record.
+__device__ __forceinline__ void store_plan(RowPlan* slot, const RowPlan& p) {
+  volatile uint32_t* w = reinterpret_cast<volatile uint32_t*>(slot);
+  w[7] = NO_TAG;
+  __threadfence_block();
+  w[0] = __float_as_uint(p.u);
+  w[1] = __float_as_uint(p.inv);
+  w[2] = __float_as_uint(p.pf);
+  w[3] = __float_as_uint(p.top_p);
+  w[4] = p.k;
+  w[5] = p.nf;
+  w[6] = p.sa;
+  __threadfence_block();
+  w[7] = p.tag;
+}
+
+__device__ __forceinline__ bool load_plan(const RowPlan* slot, uint32_t ticket, RowPlan& p) {
+  const volatile uint32_t* w = reinterpret_cast<const volatile uint32_t*>(slot);
+  if (w[7] != ticket) return false;
+  __threadfence_block();
+  p.u = __uint_as_float(w[0]);
+  p.inv = __uint_as_float(w[1]);
+  p.pf = __uint_as_float(w[2]);
+  p.top_p = __uint_as_float(w[3]);
+  p.k = w[4];
+  p.nf = w[5];
+  p.sa = w[6];
+  p.tag = ticket;
+  __threadfence_block();
+  return w[7] == ticket;
 }
 
 // Per-row transform inputs.
@@ -491,7 +554,7 @@ __device__ __forceinline__ unsigned long long pack_top_p(int status, int ns, flo
 // holds the nucleus (vocabulary order, B = exp(x - m2)).  Returns status,
 // nucleus length and m2 packed by pack_top_p.
 __device__ unsigned long long apply_top_p(float* B, float* BX, uint16_t* BI, int ns, float m1,
-                                          double top_p_d, unsigned long long* keys,
+                                          float top_p, unsigned long long* keys,
                                           uint32_t* hist) {
   const unsigned lane = lane_id();
   // Denominator: sequential f32 sum in vocabulary order.
@@ -510,7 +573,6 @@ __device__ unsigned long long apply_top_p(float* B, float* BX, uint16_t* BI, int
   __syncwarp();
   // The first position > 0 whose preceding cumulative reaches top_p starts
   // the masked tail.
-  const float top_p = (float)top_p_d;
   float cum = 0.0f;
   int pos = 0;
   unsigned long long cut = ~0ull, last = 0ull;
@@ -607,7 +669,7 @@ __device__ unsigned long long apply_top_p(float* B, float* BX, uint16_t* BI, int
 __device__ __noinline__ unsigned long long general_compute(
     float* A, float* GB, float* GBX, uint16_t* GBI, const uint32_t* bm, uint32_t* hist,
     unsigned long long* keys, int n, float inv, float pf, int use_pen, int sf, int allow,
-    unsigned top_k, double top_p, float u, unsigned char* masks, float* probs) {
+    unsigned top_k, int use_top_p, float top_p, float u, unsigned char* masks, float* probs) {
   const unsigned lane = lane_id();
   RowCtx rc;
   rc.n = n;
@@ -675,7 +737,7 @@ __device__ __noinline__ unsigned long long general_compute(
     }
     __syncwarp();
     float m2 = mx;
-    if (top_p < 1.0) {
+    if (use_top_p) {
       const unsigned long long r = apply_top_p(GB, GBX, GBI, ns, mx, top_p, keys, hist);
       const int st = (int)(r >> 56);
       if (st != Q3S_STATUS_OK) {
@@ -860,19 +922,18 @@ __device__ bool find_tau(const float (&vm)[NJ], float mx, int k, int hi, float& 
   return tau > neg_inf();
 }
 
-__device__ __forceinline__ float warp_min(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(FULL, v, o));
-  return v;
-}
-
 // Bucket of x in [lo, lo + 64/scale) for the k-th-value histogram: a
 // monotone map of x (equal values share a bucket), clamped to [0, 63].
-__device__ __forceinline__ int kbucket(float x, float lo, float scale) {
-  const float y = __fmul_rn(__fsub_rn(x, lo), scale);
-  // NaN (0 * inf) and y <= 0 go to bucket 0; truncation of y in (0, 63) is
-  // its floor.
-  return y > 0.0f ? (y >= 63.0f ? 63 : (int)y) : 0;
+// Bucket of x in an interval [a, b] with rs = 1 / (b - a): 63 - floor(64 z^4)
+// for z = (b - x) * rs, clamped to [0, 63].  Every step is a monotone f32
+// operation, so the map is monotone in x (equal values share a bucket); z^4
+// makes the buckets narrow near a, where the candidates of a top-k tail
+// crowd.  NaN (0 * inf at x = b) goes to the top bucket, as x = b does.
+__device__ __forceinline__ int kbucket(float x, float b, float rs) {
+  const float z = __fmul_rn(__fsub_rn(b, x), rs);
+  const float z2 = __fmul_rn(z, z);
+  const float m = __fmul_rn(64.0f, __fmul_rn(z2, z2));
+  return m >= 63.0f ? 0 : (m > 0.0f ? 63 - (int)m : 63);
 }
 
 // Zeroes a level of the k-th-value histogram (counts, largest and smallest
@@ -920,14 +981,20 @@ __device__ __forceinline__ int collect_cands(const RowCtx& r, uint32_t flags, fl
   __syncwarp();
   const uint32_t lt = lanemask_lt();
   int base = 0;
+  // Each lane's next vector is loaded one iteration ahead.
+  int qn = lane < NF ? (int)Qs[lane] : -1;
+  uint4 wn = qn >= 0 ? __ldg(r.g16 + qn) : make_uint4(0u, 0u, 0u, 0u);
   for (int i0 = 0; i0 < NF; i0 += 32) {
-    const int i = i0 + lane;
-    const int q = i < NF ? (int)Qs[i] : -1;
+    const int q = qn;
+    const uint4 w = wn;
+    const int inext = i0 + 32 + lane;
+    qn = inext < NF ? (int)Qs[inext] : -1;
+    if (qn >= 0) wn = __ldg(r.g16 + qn);
     float x[EPV];
     uint32_t bits = 0;
     if (q >= 0) {
       float e[EPV];
-      unpack_vec<DT>(__ldg(r.g16 + q), e);
+      unpack_vec<DT>(w, e);
 #pragma unroll
       for (int c = 0; c < EPV; ++c) {
         x[c] = xform<XF, EDGE>(e[c], q * EPV + c - r.mis, r);
@@ -1146,7 +1213,10 @@ __device__ __noinline__ unsigned long long finish_warp(const uint2* L, int c, in
 __device__ __forceinline__ float cr_expf_nonpos(float xf) {
   if (xf < -104.0f) return 0.0f;
   const double x = (double)xf;
-  const double kd = rint(__dmul_rn(x, 0x1.71547652b82fep+0));
+  // rint(x / ln2) by the 1.5 * 2^52 addition (round to nearest even, exact
+  // for |x / ln2| < 2^51); k is the low word of the sum.
+  const double big = __dadd_rn(__dmul_rn(x, 0x1.71547652b82fep+0), 0x1.8p52);
+  const double kd = __dsub_rn(big, 0x1.8p52);
   double r = __fma_rn(-kd, 0x1.62e42fefa39efp-1, x);
   r = __fma_rn(-kd, 0x1.abc9e3b39803fp-56, r);
   double p = 0x1.6124613a86d09p-33;
@@ -1163,8 +1233,8 @@ __device__ __forceinline__ float cr_expf_nonpos(float xf) {
   p = __fma_rn(p, r, 0.5);
   p = __fma_rn(p, r, 1.0);
   p = __fma_rn(p, r, 1.0);
-  const long long k = (long long)kd;
-  const double scale = __longlong_as_double((k + 1023LL) << 52);
+  const int k = __double2loint(big);
+  const double scale = __hiloint2double((k + 1023) << 20, 0);
   return __double2float_rn(__dmul_rn(p, scale));
 }
 
@@ -1247,13 +1317,12 @@ __device__ __forceinline__ unsigned long long finish_topk_hist(
         break;
       }
       const float d = __fsub_rn(b, a);
-      const float scale =
-          __fmul_rn(64.0f, __frcp_rn(d < __int_as_float(0x7f800000) ? d : 3.40282347e38f));
+      const float rs = __frcp_rn(d < __int_as_float(0x7f800000) ? d : 3.40282347e38f);
       hist_clear(h);
       __syncwarp();
       for (int j = lane; j < c; j += 32) {
         const float x = ex(L[j]);
-        if (a <= x && x <= b) hist_add(h, kbucket(x, a, scale), x);
+        if (a <= x && x <= b) hist_add(h, kbucket(x, b, rs), x);
       }
       __syncwarp();
       // Suffix counts from the top bucket down: suf = members in buckets
@@ -1298,7 +1367,7 @@ __device__ __forceinline__ unsigned long long finish_topk_hist(
           bool in = false;
           if (j < c) {
             x = ex(L[j]);
-            in = a <= x && x <= b && kbucket(x, a, scale) == B;
+            in = a <= x && x <= b && kbucket(x, b, rs) == B;
           }
           const unsigned bb = __ballot_sync(FULL, in);
           if (in) Bb[base + __popc(bb & lt)] = x;
@@ -1325,7 +1394,7 @@ __device__ __forceinline__ unsigned long long finish_topk_hist(
   }
   if (lane == 0) tsm[0] = t;
   // Survivors, compacted in place (d <= j, and every read of an iteration
-  // precedes its writes), with their softmax numerators.
+  // precedes its writes), then their softmax numerators.
   int ns = 0;
   for (int j0 = 0; j0 < c; j0 += 32) {
     const int j = j0 + lane;
@@ -1336,13 +1405,11 @@ __device__ __forceinline__ unsigned long long finish_topk_hist(
       sv = ex(en) >= t;
     }
     const unsigned bb = __ballot_sync(FULL, sv);
-    if (sv) {
-      const int d = ns + __popc(bb & lt);
-      L[d] = en;
-      Bb[d] = cr_expf_nonpos(__fsub_rn(ex(en), Mx));
-    }
+    if (sv) L[ns + __popc(bb & lt)] = en;
     ns += __popc(bb);
   }
+  __syncwarp();
+  for (int j = lane; j < ns; j += 32) Bb[j] = cr_expf_nonpos(__fsub_rn(ex(L[j]), Mx));
   if (lane < ((8 - (ns & 7)) & 7)) Bb[ns + lane] = 0.0f;  // zero-pad to a multiple of 8
   __syncwarp();
   const float sum = chain_prefix(Bb, ns);
@@ -1384,32 +1451,34 @@ __device__ void debug_masks(const void* p0, const RowCtx& r, float t, unsigned c
   __syncwarp();
 }
 
-// Fast path.  Returns false when the row must take the general path
-// instead (which reads the row from global memory).
+// Outcomes of the templated front of the fast path.
+enum { FRONT_GENERAL = 0, FRONT_DONE = 1, FRONT_LIST = 2 };
+
+// Fast path, up to the candidate list: scan, release of the stage, tau and
+// the collection.  FRONT_LIST leaves c candidates in f.list with the row
+// maximum Mx and the lower bound lo of their values (after the temperature);
+// FRONT_DONE sets `out`; FRONT_GENERAL sends the row to the general path
+// (which reads the row from global memory).
 template <int DT, int NJ, bool XF, bool EDGE>
-__device__ bool fast_row(const FastSpace& f, const StageView& s, const RowMeta& m,
-                         const RowCtx& rc, float u, Releaser& rel, float& delta, RowOut& out,
-                         const DebugRow& dbg) {
-  const q3s_row_params& P = m.P;
+__device__ int fast_front(const FastSpace& f, int k, bool use_top_p, const RowCtx& rc,
+                          Releaser& rel, float& delta, RowOut& out, int& c_out, float& Mx_out,
+                          float& lo_out) {
   float vm[NJ];
   const float mx = scan_stage<DT, NJ, XF, EDGE>(f, rc, vm);
   release<DT>(rel);  // everything below reads the row from global memory
-  if (!XF && mx == __int_as_float(0x7f800000)) return false;  // raw +inf
+  if (!XF && mx == __int_as_float(0x7f800000)) return FRONT_GENERAL;  // raw +inf
   if (mx == neg_inf() || mx != mx) {
-    release<DT>(rel);
     out = {rc.sf >= 0 ? Q3S_STATUS_SUPPRESSION_NO_CANDIDATE : Q3S_STATUS_NO_CANDIDATE, 0u};
-    return true;
+    return FRONT_DONE;
   }
   const float Mx = XF ? mx : __fmul_rn(mx, rc.inv);
   if (Mx == __int_as_float(0x7f800000)) {
-    release<DT>(rel);
     out = {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
-    return true;
+    return FRONT_DONE;
   }
-  const int k = (int)P.top_k;
   const int hi = k <= 128 ? max(2 * k, 64) : k + 96;
   float tau = mx;  // k == 1: the maximum and its ties
-  if (k > 1 && !find_tau(vm, mx, k, hi, delta, tau)) return false;
+  if (k > 1 && !find_tau(vm, mx, k, hi, delta, tau)) return FRONT_GENERAL;
   // Raw-domain selection: lower tau until its image lies strictly below the
   // image of tau, so no element below the new tau can tie the k-th largest
   // x after the multiply.
@@ -1422,40 +1491,18 @@ __device__ bool fast_row(const FastSpace& f, const StageView& s, const RowMeta& 
       t2 = __fsub_rn(t2, fmaxf(fabsf(t2) * 3.814697265625e-06f, 1.1754944e-38f));
       ok = __fmul_rn(t2, rc.inv) < img;
     }
-    if (!ok) return false;
+    if (!ok) return FRONT_GENERAL;
     tau = t2;
   }
   const uint32_t flags = chunk_flags(vm, tau);
-  const int use_top_p = P.top_p < 1.0 ? 1 : 0;
   const int c = collect_cands<DT, NJ, XF, EDGE>(rc, flags, tau,
                                                 reinterpret_cast<uint16_t*>(f.Kb), f.list);
-  if (c < k) return false;  // more than ROW_CAP candidates (or none: impossible)
-  if (use_top_p && c > 256) return false;  // the sorting finisher holds 256 keys
-  const float top_p = (float)P.top_p;
-  float* tsm = reinterpret_cast<float*>(f.hist);
-  float* Bb = reinterpret_cast<float*>(f.Kb);
-  unsigned long long r;
-  if (!use_top_p) {
-    // Every candidate lies in [lo, Mx].
-    const float lo = XF ? tau : __fmul_rn(tau, rc.inv);
-    r = finish_topk_hist(f.list, c, k, s.n, Mx, lo, u, Bb, f.hist + 16, tsm, dbg.masks,
-                         dbg.probs);
-  } else if (c <= 32) {
-    r = finish_warp<1>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, Bb, f.Kb, tsm, dbg.masks,
-                       dbg.probs);
-  } else if (c <= 128) {
-    r = finish_warp<4>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, Bb, f.Kb, tsm, dbg.masks,
-                       dbg.probs);
-  } else {
-    r = finish_warp<8>(f.list, c, k, s.n, Mx, u, use_top_p, top_p, Bb, f.Kb, tsm, dbg.masks,
-                       dbg.probs);
-  }
-  out = {(int)(r >> 32), (uint32_t)r};
-  if (dbg.masks) {
-    __syncwarp();
-    debug_masks<DT, XF>(s.p0, rc, tsm[0], dbg.masks);
-  }
-  return true;
+  if (c < k) return FRONT_GENERAL;  // more than ROW_CAP candidates (or none: impossible)
+  if (use_top_p && c > 256) return FRONT_GENERAL;  // the sorting finisher holds 256 keys
+  c_out = c;
+  Mx_out = Mx;
+  lo_out = XF ? tau : __fmul_rn(tau, rc.inv);  // every candidate lies in [lo, Mx]
+  return FRONT_LIST;
 }
 
 // Greedy row (sampling.rs:574-591) straight from the stage.
@@ -1485,44 +1532,76 @@ __device__ RowOut greedy_stage(const FastSpace& f, const StageView& s, int sf, i
 // A sampled row: fast path when it applies, else the general path.
 template <int DT, int NJ>
 __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const GenSpace& g,
-                              const RowMeta& m, const StageView& s, Releaser& rel, float& delta,
-                              const DebugRow& dbg) {
-  const q3s_row_params& P = m.P;
+                              const RowPlan& pl, int sf, int allow, const StageView& s,
+                              Releaser& rel, float& delta, const DebugRow& dbg) {
+  const uint32_t flags = pl.nf >> 16;
+  const bool use_top_p = (flags & PF_TOP_P) != 0u;
   RowCtx rc;
   rc.n = s.n;
   rc.mis = s.mis;
   rc.Q = s.Q;
   rc.g16 = s.g16;
-  rc.inv = __fdiv_rn(1.0f, (float)P.temperature);
-  rc.pf = (float)P.repetition_penalty;
-  rc.sf = P.suppress_from;
-  rc.allow = P.allow_token;
+  rc.inv = pl.inv;
+  rc.pf = pl.pf;
+  rc.sf = sf;
+  rc.allow = allow;
   rc.bm = f.bm;
-  rc.use_pen = P.repetition_penalty != 1.0 && m.h1 > m.h0;
-  const float u = a.uniform_override ? m.uo : philox_uniform(m.seed, m.subseq, P.ctr_lo);
+  rc.use_pen = (flags & PF_USE_PEN) != 0u;
+  const float u = pl.u;
   const bool inv_ok = rc.inv > 0.0f && rc.inv < __int_as_float(0x7f800000);
-  const bool fast = inv_ok && P.top_k >= 1u && P.top_k <= (uint32_t)FAST_MAX_K &&
-                    P.top_k < (uint32_t)s.n && s.Q <= 32 * NJ;
+  const bool fast = inv_ok && pl.k >= 1u && pl.k <= (uint32_t)FAST_MAX_K &&
+                    pl.k < (uint32_t)s.n && s.Q <= 32 * NJ;
   if (fast) {
     const bool xf = rc.use_pen || rc.sf >= 0;
     const bool edge = s.mis != 0 || (s.n % Elem<DT>::EPV) != 0 || s.Q != 32 * NJ;
+    const int k = (int)pl.k;
     RowOut out;
-    bool done;
+    int c = 0;
+    float Mx = 0.0f, lo = 0.0f;
+    int fr;
     if (xf)
-      done = edge ? fast_row<DT, NJ, true, true>(f, s, m, rc, u, rel, delta, out, dbg)
-                  : fast_row<DT, NJ, true, false>(f, s, m, rc, u, rel, delta, out, dbg);
+      fr = edge ? fast_front<DT, NJ, true, true>(f, k, use_top_p, rc, rel, delta, out, c, Mx, lo)
+                : fast_front<DT, NJ, true, false>(f, k, use_top_p, rc, rel, delta, out, c, Mx, lo);
     else
-      done = edge ? fast_row<DT, NJ, false, true>(f, s, m, rc, u, rel, delta, out, dbg)
-                  : fast_row<DT, NJ, false, false>(f, s, m, rc, u, rel, delta, out, dbg);
-    if (done) return out;
+      fr = edge ? fast_front<DT, NJ, false, true>(f, k, use_top_p, rc, rel, delta, out, c, Mx, lo)
+                : fast_front<DT, NJ, false, false>(f, k, use_top_p, rc, rel, delta, out, c, Mx,
+                                                   lo);
+    if (fr == FRONT_DONE) return out;
+    if (fr == FRONT_LIST) {
+      float* tsm = reinterpret_cast<float*>(f.hist);
+      float* Bb = reinterpret_cast<float*>(f.Kb);
+      unsigned long long r;
+      if (!use_top_p) {
+        r = finish_topk_hist(f.list, c, k, s.n, Mx, lo, u, Bb, f.hist + 16, tsm, dbg.masks,
+                             dbg.probs);
+      } else if (c <= 32) {
+        r = finish_warp<1>(f.list, c, k, s.n, Mx, u, 1, pl.top_p, Bb, f.Kb, tsm, dbg.masks,
+                           dbg.probs);
+      } else if (c <= 128) {
+        r = finish_warp<4>(f.list, c, k, s.n, Mx, u, 1, pl.top_p, Bb, f.Kb, tsm, dbg.masks,
+                           dbg.probs);
+      } else {
+        r = finish_warp<8>(f.list, c, k, s.n, Mx, u, 1, pl.top_p, Bb, f.Kb, tsm, dbg.masks,
+                           dbg.probs);
+      }
+      out = {(int)(r >> 32), (uint32_t)r};
+      if (dbg.masks) {
+        __syncwarp();
+        if (xf)
+          debug_masks<DT, true>(s.p0, rc, tsm[0], dbg.masks);
+        else
+          debug_masks<DT, false>(s.p0, rc, tsm[0], dbg.masks);
+      }
+      return out;
+    }
   }
   const unsigned lane = lane_id();
   release<DT>(rel);
   for (int i = lane; i < s.n; i += 32) g.A[i] = load_elem<DT>(s.p0, i);
   __syncwarp();
   const unsigned long long r = general_compute(
-      g.A, g.B, g.BX, g.BI, f.bm, reinterpret_cast<uint32_t*>(f.list), f.Kb, s.n,
-      rc.inv, rc.pf, rc.use_pen ? 1 : 0, rc.sf, rc.allow, P.top_k, P.top_p, u, dbg.masks,
+      g.A, g.B, g.BX, g.BI, f.bm, reinterpret_cast<uint32_t*>(f.list), f.Kb, s.n, rc.inv, rc.pf,
+      rc.use_pen ? 1 : 0, rc.sf, rc.allow, pl.k, use_top_p ? 1 : 0, pl.top_p, u, dbg.masks,
       dbg.probs);
   return {(int)(r >> 32), (uint32_t)r};
 }
@@ -1535,8 +1614,9 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
   const int warps = blockDim.x >> 5;
   const unsigned lane = lane_id();
   RingCtl* ctl = reinterpret_cast<RingCtl*>(smem);
+  RowPlan* plans = reinterpret_cast<RowPlan*>(smem + CTL_BYTES);
   const size_t sbytes = stage_bytes(a.vcap, es);
-  unsigned char* ring = smem + CTL_BYTES;
+  unsigned char* ring = smem + HEAD_BYTES;
   FastSpace f = carve_warp(ring + RING * sbytes + (size_t)warp * warp_bytes(a.vcap), a.vcap);
   const long long gw = (long long)blockIdx.x * warps + warp;
   const GenSpace g = carve_gen(a.scratch + (size_t)gw * gen_bytes(a.vcap), a.vcap);
@@ -1559,6 +1639,13 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
       }
     }
   }
+  // Plans of the first two batches of tickets, one thread per ticket.
+  for (int i = threadIdx.x; i < PLAN_SLOTS; i += blockDim.x)
+    reinterpret_cast<volatile uint32_t*>(&plans[i])[7] = NO_TAG;
+  if (threadIdx.x < 64) {
+    const long long row = blockIdx.x + (long long)threadIdx.x * G;
+    if (row < a.num_rows) store_plan(&plans[threadIdx.x], compute_plan(a, row, threadIdx.x));
+  }
   __syncthreads();
   float delta = __int_as_float(0x7fc00000);  // previous tau of this warp (none yet)
 #pragma unroll 1
@@ -1572,10 +1659,20 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
     const uint32_t gen = t / RING;
     f.stage = ring + slot * sbytes;
     Releaser rel{&a, ctl, f.stage, slot, blockIdx.x + (long long)(t + RING) * G, gen + 1u, false};
-    const RowMeta cur = load_meta(a, row);
-    const int n = cur.n;
-    const q3s_row_params& P = cur.P;
-    int st = row_fits(a, n) ? validate(P) : Q3S_STATUS_UNSUPPORTED;
+    // The warp that opens a batch of 32 tickets plans the batch after it,
+    // one lane per ticket.
+    if ((t & 31u) == 0u && t >= 32u) {
+      const uint32_t tp = t + 32u + lane;
+      const long long prow = blockIdx.x + (long long)tp * G;
+      if (prow < a.num_rows) store_plan(&plans[tp % PLAN_SLOTS], compute_plan(a, prow, tp));
+    }
+    RowPlan pl;
+    if (!__all_sync(FULL, load_plan(&plans[t % PLAN_SLOTS], t, pl))) pl = compute_plan(a, row, t);
+    const int n = (int)(pl.nf & 0xFFFFu);
+    const uint32_t pflags = pl.nf >> 16;
+    const int st = (int)(pflags & PF_STATUS);
+    const int sf = (int)(int16_t)(pl.sa & 0xFFFFu);
+    const int allow = (int)(int16_t)(pl.sa >> 16);
     DebugRow dbg{nullptr, nullptr};
     if (a.masks && st == Q3S_STATUS_OK) dbg.masks = a.masks + row * a.probs_stride;
     if (a.probs && st == Q3S_STATUS_OK) dbg.probs = a.probs + row * a.probs_stride;
@@ -1585,11 +1682,12 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
       for (int i = lane; i < n; i += 32) dbg.probs[i] = 0.0f;
     // History bitmap of a sampled row with a penalty (filled while the
     // stage copy may still be in flight).
-    if (st == Q3S_STATUS_OK && P.do_sample && P.repetition_penalty != 1.0 && cur.h1 > cur.h0) {
+    if (st == Q3S_STATUS_OK && (pflags & PF_USE_PEN)) {
+      const long long h0 = a.history_offsets[row], h1 = a.history_offsets[row + 1];
       const int words = (n + 31) >> 5;
       for (int w = lane; w < words; w += 32) f.bm[w] = 0u;
       __syncwarp();
-      for (long long h = cur.h0 + lane; h < cur.h1; h += 32) {
+      for (long long h = h0 + lane; h < h1; h += 32) {
         const int id = a.history[h];
         if (id < n) atomicOr(&f.bm[id >> 5], 1u << (id & 31));
       }
@@ -1611,10 +1709,10 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
     RowOut out{st, 0u};
     if (st == Q3S_STATUS_OK) {
       const StageView s = complete_stage<DT>(a, row, n, f.stage);
-      if (!P.do_sample) {
-        out = greedy_stage<DT>(f, s, P.suppress_from, P.allow_token);
+      if (!(pflags & PF_DO_SAMPLE)) {
+        out = greedy_stage<DT>(f, s, sf, allow);
       } else {
-        out = sampled_row<DT, NJ>(a, f, g, cur, s, rel, delta, dbg);
+        out = sampled_row<DT, NJ>(a, f, g, pl, sf, allow, s, rel, delta, dbg);
       }
     }
     release<DT>(rel);
