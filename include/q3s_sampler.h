@@ -145,15 +145,19 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* batch, void* stream);
  * every device that loads the library until the process exits. */
 #define Q3S_STATIC_SCRATCH_BYTES (32u * 1024u * 1024u)
 
-/* q3s_sample_batch without any device allocation: the same kernel, with its
+/* q3s_sample_batch without any device allocation, for callers that must not
+ * call cudaMalloc: an engine whose device memory belongs to its own pool
+ * allocator (a stray allocation can exceed that pool's budget), or a
+ * per-step generation loop that cannot take the device-wide synchronisation
+ * cudaMalloc / cudaFree may cause.  The same kernel runs, with its
  * general-path workspace in a file-scope device array of
  * Q3S_STATIC_SCRATCH_BYTES instead of a context allocation.  No counterpart
  * in the reference, which samples on the host (src/talker/sampling.rs) and
  * keeps no device workspace.  Same arguments and results as
  * q3s_sample_batch; in addition it rejects vocab > Q3S_MAX_VOCAB with
  * Q3S_E_INVALID_ARGUMENT, and it launches only as many blocks as the array
- * holds workspace for (about 14 bytes per vocabulary entry per warp, up to 12 warps
- * a block: 97 blocks at vocab 2048, 65 at 3072 and 4096).  The first call on
+ * holds workspace for (about 14 bytes per vocabulary entry per warp, up to
+ * 16 warps a block: 73 blocks at vocab 2048, 48 at 3072, 45 at 4096).  The first call on
  * a device looks up the array's address (cudaGetSymbolAddress, which may load
  * the module): make it before any stream capture.  Calls share the array and
  * nothing in it has to start at zero; calls whose kernels overlap on the GPU

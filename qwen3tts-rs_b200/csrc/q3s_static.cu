@@ -1,7 +1,11 @@
 // q3s_sample_batch_static: the batched sampling launch of q3s_sample_batch
 // with its general-path workspace in a file-scope device array, so that a
 // call allocates nothing (no cudaMalloc, cudaFree or allocating library
-// routine).  The kernel and its results are those of q3s_sample_batch.
+// routine).  It serves callers that must not allocate device memory while
+// they generate: engines whose device memory is owned by their own pool
+// allocator, and per-step loops that cannot take the synchronisation an
+// allocation may cause.  The kernel and its results are those of
+// q3s_sample_batch.
 //
 // The array is Q3S_STATIC_SCRATCH_BYTES (32 MiB) on every device that loads
 // the library, held until the process exits.  Its address is looked up once

@@ -1,7 +1,9 @@
-"""q3s_sample_batch_static (the entry point whose workspace is a file-scope
-device array) against q3s_sample_batch (the context-allocated workspace) on
-the same inputs, through the C ABI, two calls in a row so the second call
-runs on the workspace the first one left behind.
+"""q3s_sample_batch_static (the entry point for callers that must not
+allocate device memory during generation, e.g. engines whose device memory
+belongs to their own pool allocator; its workspace is a file-scope device
+array) against q3s_sample_batch (the context-allocated workspace) on the
+same inputs, through the C ABI, two calls in a row so the second call runs
+on the workspace the first one left behind.
 
 Bar: tokens and statuses exact, final probabilities within 1e-5 relative and
 masks exact.  This file sorts last so it also runs after every other GPU test
