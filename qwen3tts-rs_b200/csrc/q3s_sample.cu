@@ -1082,10 +1082,10 @@ __device__ __forceinline__ unsigned long long pack_out(int status, uint32_t toke
 // the statements of sampling.rs:654-729 on the candidate set, which holds
 // every value >= the k-th largest.  Sort keys are 32-bit: (~total_key(x)) for
 // the selection, (index << 16 | list position) for vocabulary order.  Writes
-// the top-k threshold to tsm[0].  Kept out of line (one copy per R) with
-// scalar and pointer arguments only.
+// the top-k threshold to tsm[0].  Inlined: an out-of-line call here makes
+// the register allocator spill around the hot path of rows without top-p.
 template <int R>
-__device__ __noinline__ unsigned long long finish_warp(const uint2* L, int c, int k, int n,
+__device__ __forceinline__ unsigned long long finish_warp(const uint2* L, int c, int k, int n,
                                                       float Mx, float u, int use_top_p,
                                                       float top_p, float* Bb,
                                                       unsigned long long* Kb, float* tsm,
@@ -1238,24 +1238,43 @@ __device__ __forceinline__ float cr_expf_nonpos(float xf) {
   return __double2float_rn(__dmul_rn(p, scale));
 }
 
-// Sequential f32 prefix sums of B[0..count) in place by lane 0 (B 16-byte
-// aligned and zero-padded to a multiple of 8); returns the total to every
-// lane.  Eight terms per step, loads one step ahead of the additions.
+// Shared-memory vector load and store through the shared window (32-bit
+// addresses), whatever address space the compiler could infer for a pointer.
+__device__ __forceinline__ float4 lds4(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(a)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void sts4(uint32_t a, const float4& v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
+// Sequential f32 prefix sums of B[0..count) in place by lane 0 (B in shared
+// memory, 16-byte aligned and zero-padded to a multiple of 8); returns the
+// total to every lane.  Eight terms per step, loads one step ahead of the
+// additions.
 __device__ __forceinline__ float chain_prefix(float* B, int count) {
   float c = 0.0f;
   if (lane_id() == 0) {
-    float4* B4 = reinterpret_cast<float4*>(B);
+    const uint32_t base = smem_u32(B);
     const int n8 = (count + 7) >> 3;
     float4 na = make_float4(0.f, 0.f, 0.f, 0.f), nb = na;
     if (n8 > 0) {
-      na = B4[0];
-      nb = B4[1];
+      na = lds4(base);
+      nb = lds4(base + 16u);
     }
     for (int q = 0; q < n8; ++q) {
       float4 va = na, vb = nb;
+      const uint32_t a = base + 32u * (uint32_t)q;
       if (q + 1 < n8) {
-        na = B4[2 * q + 2];
-        nb = B4[2 * q + 3];
+        na = lds4(a + 32u);
+        nb = lds4(a + 48u);
       }
       c = __fadd_rn(c, va.x);
       va.x = c;
@@ -1273,8 +1292,8 @@ __device__ __forceinline__ float chain_prefix(float* B, int count) {
       vb.z = c;
       c = __fadd_rn(c, vb.w);
       vb.w = c;
-      B4[2 * q] = va;
-      B4[2 * q + 1] = vb;
+      sts4(a, va);
+      sts4(a + 16u, vb);
     }
   }
   __syncwarp();
