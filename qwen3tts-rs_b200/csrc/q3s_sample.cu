@@ -1549,10 +1549,14 @@ __device__ RowOut greedy_stage(const FastSpace& f, const StageView& s, int sf, i
 }
 
 // A sampled row: fast path when it applies, else the general path.
-template <int DT, int NJ>
+// DBG: the launch fills the debug outputs (probs, masks).  Production
+// launches compile without that code, which would otherwise weigh on the
+// register allocation of the hot path.
+template <int DT, int NJ, bool DBG>
 __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const GenSpace& g,
                               const RowPlan& pl, int sf, int allow, const StageView& s,
-                              Releaser& rel, float& delta, const DebugRow& dbg) {
+                              Releaser& rel, float& delta, const DebugRow& dbg_in) {
+  const DebugRow dbg{DBG ? dbg_in.masks : nullptr, DBG ? dbg_in.probs : nullptr};
   const uint32_t flags = pl.nf >> 16;
   const bool use_top_p = (flags & PF_TOP_P) != 0u;
   RowCtx rc;
@@ -1625,7 +1629,7 @@ __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const Gen
   return {(int)(r >> 32), (uint32_t)r};
 }
 
-template <int DT, int NJ>
+template <int DT, int NJ, bool DBG>
 __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int es = Elem<DT>::BYTES;
@@ -1693,8 +1697,8 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
     const int sf = (int)(int16_t)(pl.sa & 0xFFFFu);
     const int allow = (int)(int16_t)(pl.sa >> 16);
     DebugRow dbg{nullptr, nullptr};
-    if (a.masks && st == Q3S_STATUS_OK) dbg.masks = a.masks + row * a.probs_stride;
-    if (a.probs && st == Q3S_STATUS_OK) dbg.probs = a.probs + row * a.probs_stride;
+    if (DBG && a.masks && st == Q3S_STATUS_OK) dbg.masks = a.masks + row * a.probs_stride;
+    if (DBG && a.probs && st == Q3S_STATUS_OK) dbg.probs = a.probs + row * a.probs_stride;
     if (dbg.masks)
       for (int i = lane; i < n; i += 32) dbg.masks[i] = 0;
     if (dbg.probs)
@@ -1731,7 +1735,7 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
       if (!(pflags & PF_DO_SAMPLE)) {
         out = greedy_stage<DT>(f, s, sf, allow);
       } else {
-        out = sampled_row<DT, NJ>(a, f, g, pl, sf, allow, s, rel, delta, dbg);
+        out = sampled_row<DT, NJ, DBG>(a, f, g, pl, sf, allow, s, rel, delta, dbg);
       }
     }
     release<DT>(rel);
@@ -1795,14 +1799,20 @@ __global__ void greedy_kernel(const void* logits, long long num_rows, long long 
   }
 }
 
-template <int DT, int NJ>
-cudaError_t launch_t(const KernelArgs& a, int grid, int warps, cudaStream_t stream) {
+template <int DT, int NJ, bool DBG>
+cudaError_t launch_dbg(const KernelArgs& a, int grid, int warps, cudaStream_t stream) {
   const size_t smem = block_smem(a.vcap, Elem<DT>::BYTES, warps);
-  cudaError_t e = cudaFuncSetAttribute(sample_kernel<DT, NJ>,
+  cudaError_t e = cudaFuncSetAttribute(sample_kernel<DT, NJ, DBG>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  sample_kernel<DT, NJ><<<grid, warps * 32, smem, stream>>>(a);
+  sample_kernel<DT, NJ, DBG><<<grid, warps * 32, smem, stream>>>(a);
   return cudaGetLastError();
+}
+
+template <int DT, int NJ>
+cudaError_t launch_t(const KernelArgs& a, int grid, int warps, cudaStream_t stream) {
+  if (a.probs || a.masks) return launch_dbg<DT, NJ, true>(a, grid, warps, stream);
+  return launch_dbg<DT, NJ, false>(a, grid, warps, stream);
 }
 
 }  // namespace

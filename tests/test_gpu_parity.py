@@ -380,6 +380,23 @@ def test_full_size_bandwidth(k):
     np.testing.assert_array_equal(t.cpu().numpy().view(np.uint32)[rows], ref["tokens"])
 
 
+def test_hetero_production_kernel_matches_oracle():
+    """The launch without debug outputs compiles its own kernel (no debug
+    code on the hot path): check its tokens and statuses on a mixed batch
+    (top-p, penalties, suppression, two vocabularies)."""
+    w = workloads.hetero(DEV, streams=256)
+    args = w.device_args(DEV)
+    t, s = q3s.sample_batch(w.logits, args.pop("params"), args.pop("seeds"), args.pop("subseqs"),
+                            **args)
+    torch.cuda.synchronize()
+    rows = np.sort(np.random.default_rng(7).choice(w.num_rows, 1024, replace=False))
+    logits, offsets, vocab, params, seeds, subseqs, hist, hoff = w.oracle_layout(rows)
+    ref = oracle.sample_rows(logits, offsets, vocab, params, seeds, subseqs, hist, hoff,
+                             nthreads=oracle.cpu_count())
+    np.testing.assert_array_equal(s.cpu().numpy()[rows], ref["status"])
+    np.testing.assert_array_equal(t.cpu().numpy().view(np.uint32)[rows], ref["tokens"])
+
+
 def test_full_size_hetero_sample():
     w = workloads.hetero(DEV, streams=4096)
     rows = np.sort(np.random.default_rng(5).choice(w.num_rows, 1024, replace=False))
