@@ -37,10 +37,10 @@ TOP_K = 50
 # the Philox seed and subsequence (8 + 8), the token (4) and the status (1).
 BYTES_PER_ROW = 4 * VOCAB + 16 + 4 + 1
 # DRAM bytes (read + write) per 65,536-row launch of the sampling kernel: the
-# ncu capture of a 16,384-row launch (205.8 MB, summarised in
+# ncu capture of a 16,384-row launch (210.2 MB, summarised in
 # profiles/sample_kernel_bandwidth_16384x3072_k50_full.md) scaled by the rows,
 # since every row is read from HBM exactly once.
-NCU_TRAFFIC_PER_LAUNCH = 205.803008e6 * 4
+NCU_TRAFFIC_PER_LAUNCH = 210.206208e6 * 4
 FALLBACK_HBM_GBS = 6650.0
 
 
