@@ -429,6 +429,27 @@ def secondary(ctx, dev, q3s, workloads, np, torch):
             q3s.sample_batch(x[g], pc, sc[g * 64:(g + 1) * 64], uc[g * 64:(g + 1) * 64], ctx=ctx)
     ms = time_launches(frame, 20)
     out["cp_frame_64x15"] = {"us_per_group": ms * 1e3 / 15, "rows_per_s": 960 / (ms / 1e3)}
+    # Codebook embedding sum after sampling: 4096 streams, 16 codebooks
+    # (3072 + 15 x 2048 ids), hidden 2048, bf16, a text row per stream.
+    R, H = 4096, 2048
+    g = torch.Generator(device=dev).manual_seed(5)
+    vocabs = [3072] + [2048] * 15
+    tables = [(torch.randn((v, H), device=dev, generator=g) * 0.05).to(torch.bfloat16)
+              for v in vocabs]
+    codes = torch.stack([torch.randint(0, v, (R,), device=dev, generator=g, dtype=torch.int32)
+                         for v in vocabs], 1)
+    text = torch.randn((R, H), device=dev, generator=g).to(torch.bfloat16)
+    eout = (torch.empty((R, H), device=dev, dtype=torch.bfloat16),
+            torch.empty(R, device=dev, dtype=torch.uint8))
+    ms = time_launches(lambda: q3s.embed_sum(codes, tables, text, ctx=ctx, out=eout), 50)
+    if not bool((eout[1] == 0).all()):
+        raise RuntimeError("embedding sum failed")
+    ebytes = R * (16 * H * 2 + H * 2 + H * 2 + 16 * 4 + 1)
+    out["embed_sum_4096x16_h2048_bf16"] = {"us_per_launch": ms * 1e3,
+                                           "rows_per_s": R / (ms / 1e3),
+                                           "gbs": ebytes / (ms / 1e3) / 1e9,
+                                           "tables_mb": sum(v * H * 2 for v in vocabs) / 1e6}
+    del tables, text, eout
     # Single-stream talker step through the stateful Sampler (host round trip).
     ws = workloads.talker_single(dev, steps=200)
     s = q3s.Sampler(42, ctx)

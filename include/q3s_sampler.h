@@ -54,6 +54,7 @@ extern "C" {
 #define Q3S_STATUS_NO_CANDIDATE 5
 #define Q3S_STATUS_INVALID_DENOMINATOR 6
 #define Q3S_STATUS_UNSUPPORTED 7 /* vocabulary larger than Q3S_MAX_VOCAB */
+#define Q3S_STATUS_INVALID_CODE 8 /* q3s_embed_sum: a code outside its codebook (row zeroed) */
 #define Q3S_STATUS_NOT_RUN 255   /* row was never reached (internal error) */
 
 /* Largest vocabulary one row may have (the codec vocabularies are 3072 and 2048). */
@@ -122,6 +123,28 @@ typedef struct q3s_batch {
   int64_t probs_stride;
 } q3s_batch;
 
+/* Codebook embedding sum after sampling (talker.rs:568-580): for each row,
+ * out = ((T0[c0] + T1[c1]) + ... + T(G-1)[c(G-1)]) + text, every addition
+ * rounded to the element type, in that order.  T0 is the talker's codec
+ * embedding (codebook 0), T1.. the code predictor's codebook embeddings;
+ * text is the trailing text hidden state or tts_pad. */
+#define Q3S_MAX_CODE_GROUPS 32
+
+typedef struct q3s_embed_batch {
+  int32_t dtype;              /* Q3S_DTYPE_F32 or Q3S_DTYPE_BF16 (tables, text and out) */
+  int32_t groups;             /* G, 1..Q3S_MAX_CODE_GROUPS (16 for the 12 Hz models) */
+  int32_t hidden;             /* H, elements per embedding row */
+  int32_t reserved;
+  int64_t num_rows;           /* R */
+  const uint32_t* codes;      /* [R, G], row-major */
+  const void* const* tables;  /* HOST array of G device pointers; table g is [vocab[g], H] */
+  const int32_t* vocab;       /* HOST array [G] */
+  const void* text;           /* [R, H] (or one row), added last; NULL for none */
+  int64_t text_stride;        /* elements between text rows; 0 broadcasts one row */
+  void* out;                  /* [R, H] */
+  uint8_t* status;            /* [R]: Q3S_STATUS_OK, or Q3S_STATUS_INVALID_CODE */
+} q3s_embed_batch;
+
 /* ---- library / context --------------------------------------------------- */
 typedef struct q3s_context q3s_context;
 
@@ -163,6 +186,14 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* batch, void* stream);
  * nothing in it has to start at zero; calls whose kernels overlap on the GPU
  * race on it, so order them on one stream or with events. */
 int q3s_sample_batch_static(q3s_context* ctx, const q3s_batch* batch, void* stream);
+
+/* The embedding sum of many rows (streams) in one launch, on the device that
+ * holds the sampled codes.  Replaces, per row, the embedding_lookup and
+ * tensor additions of talker.rs:568-580 (embedding_lookup:
+ * src/talker/primitives.rs:17-25).  A row with a code at or beyond its
+ * codebook's vocabulary gets status Q3S_STATUS_INVALID_CODE and zeros
+ * (the reference's index_select fails there). */
+int q3s_embed_sum(q3s_context* ctx, const q3s_embed_batch* batch, void* stream);
 
 /* Greedy argmax with the talker reserved-token mask, many rows, on device.
  * mode Q3S_GREEDY_SELECT follows greedy_select (sampling.rs:40-60): first

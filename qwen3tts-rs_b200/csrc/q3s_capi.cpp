@@ -114,6 +114,8 @@ const char* q3s_status_message(int status) {
       return "invalid softmax denominator";
     case Q3S_STATUS_UNSUPPORTED:
       return "vocabulary larger than the sampler supports";
+    case Q3S_STATUS_INVALID_CODE:
+      return "embedding code outside its codebook";
     default:
       return "row not processed";
   }

@@ -42,6 +42,8 @@ STATUS_SUPPRESSION_NO_CANDIDATE = 4
 STATUS_NO_CANDIDATE = 5
 STATUS_INVALID_DENOMINATOR = 6
 STATUS_UNSUPPORTED = 7
+STATUS_INVALID_CODE = 8
+MAX_CODE_GROUPS = 32
 MAX_VOCAB = 4096
 
 DTYPE_F32 = 0
@@ -91,6 +93,15 @@ class _Batch(ctypes.Structure):
     ]
 
 
+class _EmbedBatch(ctypes.Structure):
+    _fields_ = [
+        ("dtype", ctypes.c_int32), ("groups", ctypes.c_int32), ("hidden", ctypes.c_int32),
+        ("reserved", ctypes.c_int32), ("num_rows", ctypes.c_int64), ("codes", ctypes.c_void_p),
+        ("tables", ctypes.c_void_p), ("vocab", ctypes.c_void_p), ("text", ctypes.c_void_p),
+        ("text_stride", ctypes.c_int64), ("out", ctypes.c_void_p), ("status", ctypes.c_void_p),
+    ]
+
+
 class _Diagnostics(ctypes.Structure):
     _fields_ = [("call_count", ctypes.c_uint32), ("sampled_calls", ctypes.c_uint32),
                 ("greedy_calls", ctypes.c_uint32), ("history_nonempty_calls", ctypes.c_uint32),
@@ -108,6 +119,7 @@ EXPORTED_SYMBOLS = (
     "q3s_sampler_destroy", "q3s_sampler_subsequence_counter",
     "q3s_sampler_set_subsequence_counter", "q3s_sampler_get_diagnostics",
     "q3s_sampler_sample_with_mode", "q3s_sampler_sample", "q3s_sample_batch_static",
+    "q3s_embed_sum",
 )
 
 _lib = None
@@ -139,6 +151,7 @@ def load(path: Optional[os.PathLike] = None):
     L.q3s_sample_batch.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Batch), ctypes.c_void_p]
     L.q3s_sample_batch_static.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Batch),
                                           ctypes.c_void_p]
+    L.q3s_embed_sum.argtypes = [ctypes.c_void_p, ctypes.POINTER(_EmbedBatch), ctypes.c_void_p]
     L.q3s_greedy_batch.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
@@ -355,6 +368,73 @@ def _launch_batch(entry: str, logits, params, seeds, subseqs, *, row_offsets, ro
     if debug:
         return tokens, status, probs, masks
     return tokens, status
+
+
+def embed_sum(codes, tables, text=None, *, ctx: Optional[Context] = None, stream=None,
+              out=None):
+    """The codebook embedding sum after sampling (q3s_embed_sum, talker.rs:568-580).
+
+    codes: CUDA int32/uint32 tensor [R, G]; tables: G CUDA tensors [vocab_g, H]
+    of one dtype (float32 or bfloat16); text: None, a [H] tensor (broadcast)
+    or [R, H].  Returns (out [R, H] in the tables' dtype, status uint8 [R]);
+    a row with a code outside its codebook has status STATUS_INVALID_CODE and
+    zeros."""
+    import torch
+    if codes.dim() != 2:
+        raise ValueError("codes must be [R, G]")
+    if codes.dtype not in (torch.int32, torch.uint32):
+        raise TypeError("codes must be int32 or uint32")
+    R, G = codes.shape
+    if len(tables) != G or G < 1 or G > MAX_CODE_GROUPS:
+        raise ValueError("one table per code group (1..32)")
+    dt = tables[0].dtype
+    if dt == torch.float32:
+        dcode = DTYPE_F32
+    elif dt == torch.bfloat16:
+        dcode = DTYPE_BF16
+    else:
+        raise TypeError("tables must be float32 or bfloat16")
+    H = int(tables[0].shape[1])
+    for t in tables:
+        if t.dtype != dt or t.dim() != 2 or int(t.shape[1]) != H or t.stride(1) != 1:
+            raise ValueError("tables must share dtype and width and have contiguous rows")
+        if t.stride(0) != H:
+            raise ValueError("tables must be contiguous")
+    dev = codes.device
+    codes = codes.contiguous()
+    stride = 0
+    if text is not None:
+        if text.dtype != dt:
+            raise TypeError("text must have the tables' dtype")
+        if text.dim() == 1:
+            stride = 0
+        else:
+            if text.shape[0] != R or text.stride(1) != 1:
+                raise ValueError("text must be [H] or [R, H] with contiguous rows")
+            stride = text.stride(0)
+    ctx = ctx or default_context(dev.index)
+    if out is None:
+        res = torch.empty((R, H), dtype=dt, device=dev)
+        status = torch.empty(R, dtype=torch.uint8, device=dev)
+    else:
+        res, status = out
+    ptrs = (ctypes.c_void_p * G)(*[t.data_ptr() for t in tables])
+    vocab = (ctypes.c_int32 * G)(*[int(t.shape[0]) for t in tables])
+    b = _EmbedBatch()
+    b.dtype = dcode
+    b.groups = G
+    b.hidden = H
+    b.num_rows = R
+    b.codes = codes.data_ptr()
+    b.tables = ctypes.cast(ptrs, ctypes.c_void_p)
+    b.vocab = ctypes.cast(vocab, ctypes.c_void_p)
+    b.text = _dptr(text)
+    b.text_stride = stride
+    b.out = res.data_ptr()
+    b.status = status.data_ptr()
+    s = torch.cuda.current_stream(dev).cuda_stream if stream is None else stream
+    _check(load().q3s_embed_sum(ctx.handle, ctypes.byref(b), ctypes.c_void_p(s)), "q3s_embed_sum")
+    return res, status
 
 
 def greedy_batch(logits, suppress_from=None, allow_token=None, mode: int = GREEDY_SELECT,

@@ -50,6 +50,7 @@ def test_abi_version_and_status_messages():
         q3s.STATUS_SUPPRESSION_NO_CANDIDATE: "suppression left no finite candidate",
         q3s.STATUS_NO_CANDIDATE: "no finite sampling candidate",
         q3s.STATUS_INVALID_DENOMINATOR: "invalid softmax denominator",
+        q3s.STATUS_INVALID_CODE: "embedding code outside its codebook",
     }
     for st, msg in expect.items():
         assert q3s.status_message(st) == msg
@@ -65,11 +66,13 @@ def test_struct_layouts_match_binding(tmp_path):
 #include <stdio.h>
 #include "q3s_sampler.h"
 int main(void) {
-  printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\n", sizeof(q3s_row_params),
+  printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\n", sizeof(q3s_row_params),
          offsetof(q3s_row_params, top_k), offsetof(q3s_row_params, do_sample),
          offsetof(q3s_row_params, suppress_from), offsetof(q3s_row_params, allow_token),
          offsetof(q3s_row_params, ctr_lo), sizeof(q3s_batch), offsetof(q3s_batch, probs_stride),
-         sizeof(q3s_sampling_options), sizeof(q3s_sampler_diagnostics));
+         sizeof(q3s_sampling_options), sizeof(q3s_sampler_diagnostics),
+         sizeof(q3s_embed_batch), offsetof(q3s_embed_batch, text_stride),
+         offsetof(q3s_embed_batch, status));
   return 0;
 }
 ''')
@@ -83,7 +86,8 @@ int main(void) {
                    dt.fields["suppress_from"][1], dt.fields["allow_token"][1],
                    dt.fields["ctr_lo"][1], ctypes.sizeof(q3s._Batch),
                    q3s._Batch.probs_stride.offset, ctypes.sizeof(q3s._Options),
-                   ctypes.sizeof(q3s._Diagnostics)]
+                   ctypes.sizeof(q3s._Diagnostics), ctypes.sizeof(q3s._EmbedBatch),
+                   q3s._EmbedBatch.text_stride.offset, q3s._EmbedBatch.status.offset]
 
 
 def test_context_without_device_fails_cleanly():
