@@ -100,6 +100,45 @@ __device__ __forceinline__ void store1(void* base, long long off, float v) {
     static_cast<uint16_t*>(base)[off] = to_bf(v);
 }
 
+// Raw 16-byte vectors of one group's 8 elements (two for f32, one for bf16).
+template <int DT>
+struct Raw {
+  static constexpr int N = DT == Q3S_DTYPE_F32 ? 2 : 1;
+  uint4 w[N];
+};
+
+template <int DT>
+__device__ __forceinline__ void load_raw(const void* base, long long off, Raw<DT>& r) {
+  const uint4* p = reinterpret_cast<const uint4*>(static_cast<const unsigned char*>(base) +
+                                                  off * (DT == Q3S_DTYPE_F32 ? 4 : 2));
+#pragma unroll
+  for (int i = 0; i < Raw<DT>::N; ++i) r.w[i] = __ldg(p + i);
+}
+
+// acc[e] + element e of r, rounded to the element type, e = 0..7 in order.
+template <int DT>
+__device__ __forceinline__ void add_raw(float (&acc)[EMBED_VEC], const Raw<DT>& r) {
+  float v[EMBED_VEC];
+  if (DT == Q3S_DTYPE_F32) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      v[4 * i] = __uint_as_float(r.w[i].x);
+      v[4 * i + 1] = __uint_as_float(r.w[i].y);
+      v[4 * i + 2] = __uint_as_float(r.w[i].z);
+      v[4 * i + 3] = __uint_as_float(r.w[i].w);
+    }
+  } else {
+    const uint32_t u[4] = {r.w[0].x, r.w[0].y, r.w[0].z, r.w[0].w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      v[2 * t] = bf((uint16_t)(u[t] & 0xFFFFu));
+      v[2 * t + 1] = bf((uint16_t)(u[t] >> 16));
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < EMBED_VEC; ++e) acc[e] = add_t<DT>(acc[e], v[e]);
+}
+
 // VEC_OK: every table, the text and the output start 16-byte aligned and H
 // is a multiple of 8, so whole 8-element vectors are aligned.
 template <int DT, bool VEC_OK>
@@ -125,11 +164,18 @@ __global__ void __launch_bounds__(EMBED_THREADS) embed_sum_kernel(const EmbedArg
         float acc[EMBED_VEC];
         if (ok) {
           load8<DT>(a.tables[0], rowoff[0] + h, acc);
-          for (int g = 1; g < G; ++g) {
-            float v[EMBED_VEC];
-            load8<DT>(a.tables[g], rowoff[g] + h, v);
+          // The next NB groups' vectors are all loaded before their adds, so
+          // NB gathers are in flight per thread; the adds keep group order.
+          constexpr int NB = 8 / Raw<DT>::N;
+#pragma unroll 1
+          for (int g0 = 1; g0 < G; g0 += NB) {
+            Raw<DT> r[NB];
 #pragma unroll
-            for (int e = 0; e < EMBED_VEC; ++e) acc[e] = add_t<DT>(acc[e], v[e]);
+            for (int j = 0; j < NB; ++j)
+              if (g0 + j < G) load_raw<DT>(a.tables[g0 + j], rowoff[g0 + j] + h, r[j]);
+#pragma unroll
+            for (int j = 0; j < NB; ++j)
+              if (g0 + j < G) add_raw<DT>(acc, r[j]);
           }
           if (a.text) {
             float v[EMBED_VEC];
