@@ -6,18 +6,24 @@
 Workload (per GPU, weak scaling): the bandwidth configuration, 65536 rows x
 3072 f32 logits ~ N(0, 1), top_k 50, top_p 1.0, temperature 1.0, no penalty;
 one step = one fused sampling launch over the 65536 rows.  The logits (805 MB)
-exceed the 126 MB L2, so consecutive steps stream them from HBM.
+exceed the 126 MB L2, so consecutive steps stream them from HBM.  Launches go
+through a prepared q3s_batch (one C call per step), so the host keeps the
+stream full and the per-step CUDA events time the kernel, not the host.
 
 `value` is whole-job rows/s with the inputs resident in HBM.  `e2e` is the same
 metric through the C ABI with host buffers: each step copies the logits and
 the per-row seeds from pinned host memory and the tokens and status bytes
-back.  `--impl reference` times the CPU restatement of the reference sampler
+back.  `results.hetero_decode_step` is the heterogeneous full decode step
+(4096 streams x 16 rows in total, whole streams sharded over the N GPUs, L2
+flushed between launches), checked against the oracle on every rank.
+`--impl reference` times the CPU restatement of the reference sampler
 (src/talker/sampling.rs, with glibc expf as Rust's f32::exp uses on Linux) on
 the host cores, rank 0 only.
 """
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -33,15 +39,17 @@ METRIC = "sampled rows/sec at vocab 3072, B=1024 and 65536 (1/2/4/8 B200); % HBM
 ROWS = 65536
 VOCAB = 3072
 TOP_K = 50
+HETERO_STREAMS = 4096
 # Algorithmic bytes per row of the bandwidth workload: 3072 f32 logits,
 # the Philox seed and subsequence (8 + 8), the token (4) and the status (1).
 BYTES_PER_ROW = 4 * VOCAB + 16 + 4 + 1
-# DRAM bytes (read + write) per 65,536-row launch of the sampling kernel: the
-# ncu capture of a 16,384-row launch (210.2 MB, summarised in
-# profiles/sample_kernel_bandwidth_16384x3072_k50_full.md) scaled by the rows,
-# since every row is read from HBM exactly once.
+# DRAM bytes (read + write) per 65,536-row launch of the sampling kernel: an
+# ncu capture of a 16,384-row launch (dram__bytes_read.sum +
+# dram__bytes_write.sum = 210.2 MB) scaled by the rows, since every row is
+# read from HBM exactly once.
 NCU_TRAFFIC_PER_LAUNCH = 210.206208e6 * 4
 FALLBACK_HBM_GBS = 6650.0
+L2_FLUSH_BYTES = 256 << 20
 
 
 def measured_peak_gbs():
@@ -53,62 +61,70 @@ def measured_peak_gbs():
 
 
 class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML while running."""
+    """Samples the SM clock and throttle reasons of the given GPUs (NVML, one
+    thread in one process) while running."""
 
     REASONS = {
         "hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
         "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80,
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.01):
-        self.samples = []
+    def __init__(self, bus_ids, period_s: float = 0.02):
+        self.samples = {i: [] for i in range(len(bus_ids))}
         self.max_mhz = None
         self._stop = threading.Event()
-        self._h = None
+        self._h = []
         self.period = period_s
         try:
             import pynvml
             pynvml.nvmlInit()
             self._nv = pynvml
-            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            for k, bus in enumerate(bus_ids):
+                try:
+                    h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+                except Exception:
+                    h = pynvml.nvmlDeviceGetHandleByIndex(k)
+                self._h.append(h)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h[0], pynvml.NVML_CLOCK_SM)
         except Exception:
-            self._h = None
+            self._h = []
         self._t = threading.Thread(target=self._run, daemon=True)
 
     def _run(self):
         nv = self._nv
         while not self._stop.is_set():
-            try:
-                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
-                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-                util = nv.nvmlDeviceGetUtilizationRates(self._h).gpu
-                self.samples.append((mhz, reasons, util))
-            except Exception:
-                pass
+            for i, h in enumerate(self._h):
+                try:
+                    mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples[i].append((mhz, reasons))
+                except Exception:
+                    pass
             time.sleep(self.period)
 
     def __enter__(self):
-        if self._h is not None:
+        if self._h:
             self._t.start()
         return self
 
     def __exit__(self, *exc):
         self._stop.set()
-        if self._h is not None:
+        if self._h:
             self._t.join()
 
     def summary(self):
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [],
-                    "samples": 0}
-        mhz = [s[0] for s in self.samples]
+        allm = [s[0] for v in self.samples.values() for s in v]
+        if not allm:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
         active = 0
-        for s in self.samples:
-            active |= s[1]
+        for v in self.samples.values():
+            for s in v:
+                active |= s[1]
         reasons = [name for name, bit in self.REASONS.items() if active & bit]
-        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz,
-                "reasons": reasons, "samples": len(self.samples)}
+        per_gpu = [statistics.median([s[0] for s in v]) if v else None
+                   for v in self.samples.values()]
+        return {"sm_mhz": statistics.median(allm), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(allm), "per_gpu_sm_mhz": per_gpu}
 
 
 def dist_setup():
@@ -126,8 +142,12 @@ def cpu_threads() -> int:
 
 
 def oracle_mod():
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import oracle  # CPU baseline / reference arm only
+    """The oracle (CPU restatement of the reference): the checker and the CPU
+    baseline, always outside the timed regions."""
+    for p in (ROOT / "oracle",):
+        if str(p) not in sys.path:
+            sys.path.insert(0, str(p))
+    import oracle
     return oracle
 
 
@@ -140,7 +160,6 @@ def cpu_rows_per_s(oracle, logits, vocab, params, target_s: float, threads: int)
     voc = np.full(R, vocab, np.int32)
     seeds = np.arange(R, dtype=np.uint64)
     sub = np.zeros(R, np.uint64)
-    # Size the sample from a short probe.
     probe = min(R, max(64, 16 * threads))
     t0 = time.perf_counter()
     oracle.sample_rows(flat, off[:probe], voc[:probe], params, seeds[:probe], sub[:probe],
@@ -215,6 +234,38 @@ def workload_config(rows: int = ROWS):
             "parallelism": "row shards, no collective"}
 
 
+class L2Flush:
+    """Writes a buffer larger than L2 (between timed launches whose inputs
+    would otherwise stay cached)."""
+
+    def __init__(self, torch, dev):
+        self.buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        self.buf.fill_(1.0)
+
+
+def time_each(torch, launch, iters, flush=None, stream=None):
+    """Mean device time of `launch` in ms: CUDA events around each launch on
+    `stream`, with an optional L2 flush before each (outside the events)."""
+    stream = stream or torch.cuda.current_stream()
+    for _ in range(3):
+        if flush:
+            flush()
+        launch()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(iters)]
+    for a, b in ev:
+        if flush:
+            flush()
+        a.record(stream)
+        launch()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in ev) / iters
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -223,6 +274,7 @@ def main() -> int:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--hetero-steps", type=int, default=100)
     ap.add_argument("--rows", type=int, default=ROWS,
                     help="rows per GPU (smaller cases are for profiler captures only)")
     args = ap.parse_args()
@@ -242,8 +294,7 @@ def main() -> int:
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     def barrier():
         if world > 1:
@@ -252,44 +303,75 @@ def main() -> int:
     def max_over_ranks(v: float) -> float:
         return shard.max_over_ranks(v, device=dev)
 
+    def gather(obj):
+        if world == 1:
+            return [obj]
+        out = [None] * world
+        dist.all_gather_object(out, obj)
+        return out
+
     ctx = q3s.Context(local)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
     w = workloads.bandwidth(dev, rows=rows, top_k=TOP_K, seed=3 + rank)
     a = w.device_args(dev)
     params, seeds, subseqs = a["params"], a["seeds"], a["subseqs"]
     tokens = torch.empty(rows, dtype=torch.int32, device=dev)
     status = torch.empty(rows, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream(dev)
-
-    def launch():
-        q3s.sample_batch(w.logits, params, seeds, subseqs, ctx=ctx, out=(tokens, status))
+    launch = q3s.prepare_batch(w.logits, params, seeds, subseqs, ctx=ctx, out=(tokens, status))
 
     for _ in range(max(args.warmup, 3)):
-        launch()
+        launch(sh)
     torch.cuda.synchronize()
     if not bool((status == 0).all()):
         raise RuntimeError("sampling failed on the benchmark workload")
 
+    props = torch.cuda.get_device_properties(dev)
+    bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+    buses = gather(bus)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     t_begin = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    host_ns = 0
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
+    sampler = ClockSampler(buses) if rank == 0 else contextlib.nullcontext()
+    with sampler as clocks:
         t_begin.record(stream)
         for i in range(args.steps):
             starts[i].record(stream)
-            launch()
+            h0 = time.perf_counter_ns()
+            launch(sh)
+            host_ns += time.perf_counter_ns() - h0
             ends[i].record(stream)
         t_end.record(stream)
         torch.cuda.synchronize()
     barrier()
-    elapsed_ms = max_over_ranks(t_begin.elapsed_time(t_end))
-    kernel_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / max(args.steps, 1)
-    kernel_ms = max_over_ranks(kernel_ms)
+    my_elapsed = t_begin.elapsed_time(t_end)
+    ks = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    gaps = [ends[i].elapsed_time(starts[i + 1]) for i in range(args.steps - 1)]
+    my_kernel = sum(ks) / max(args.steps, 1)
+    elapsed_ms = max_over_ranks(my_elapsed)
+    kernel_ms = max_over_ranks(my_kernel)
     value = shard.whole_job_rate(rows, world, args.steps, elapsed_ms)
     peak, peak_kind = measured_peak_gbs()
     achieved = rows * BYTES_PER_ROW / (kernel_ms / 1e3) / 1e9
+    per_rank = gather({
+        "rank": rank, "elapsed_ms": my_elapsed, "kernel_ms_mean": my_kernel,
+        "kernel_ms_median": statistics.median(ks), "kernel_ms_max": max(ks),
+        "gap_ms_mean": (sum(gaps) / len(gaps)) if gaps else 0.0,
+        "host_enqueue_us_mean": host_ns / 1e3 / max(args.steps, 1)})
+
+    # Parity on every rank, outside the timed region: a row sample of this
+    # rank's shard against the oracle (bit-exact tokens and statuses).
+    oracle = oracle_mod()
+    sel = np.sort(np.random.default_rng(100 + rank).choice(rows, min(rows, 256),
+                                                             replace=False))
+    ref = oracle.sample_rows(*w.oracle_layout(sel), nthreads=max(1, cpu_threads() // world))
+    my_ok = bool(np.array_equal(status.cpu().numpy()[sel], ref["status"]) and
+                 np.array_equal(tokens.cpu().numpy().view(np.uint32)[sel], ref["tokens"]))
+    parity = gather(my_ok)
 
     # End to end through the C ABI with host buffers.
     e2e = None
@@ -306,6 +388,12 @@ def main() -> int:
         chunks = 8
         cr = rows // chunks
         streams = [torch.cuda.Stream(dev) for _ in range(2)]
+        chunk_launch = []
+        for c in range(chunks):
+            sl = slice(c * cr, (c + 1) * cr)
+            chunk_launch.append(q3s.prepare_batch(dev_logits[sl], params, dev_seeds[sl],
+                                                  dev_sub[sl], ctx=ctx,
+                                                  out=(tokens[sl], status[sl])))
 
         def e2e_step():
             ev0 = torch.cuda.Event()
@@ -318,9 +406,7 @@ def main() -> int:
                     dev_logits[sl].copy_(host_logits[sl], non_blocking=True)
                     dev_seeds[sl].copy_(host_seeds[sl], non_blocking=True)
                     dev_sub[sl].copy_(host_sub[sl], non_blocking=True)
-                    q3s.sample_batch(dev_logits[sl], params, dev_seeds[sl], dev_sub[sl],
-                                     ctx=ctx, stream=s.cuda_stream,
-                                     out=(tokens[sl], status[sl]))
+                    chunk_launch[c](s.cuda_stream)
                     host_tok[sl].copy_(tokens[sl], non_blocking=True)
                     host_st[sl].copy_(status[sl], non_blocking=True)
             for s in streams:
@@ -343,22 +429,35 @@ def main() -> int:
         e2e = {"value": world * rows / (e2e_ms / 1e3), "unit": "rows/s",
                "h2d_bytes_per_step": rows * (4 * VOCAB + 16),
                "d2h_bytes_per_step": rows * 5, "ms_per_step": e2e_ms}
-        del host_logits, dev_logits
+        del host_logits, dev_logits, chunk_launch
 
-    results = {}
+    del w, launch
+    torch.cuda.empty_cache()
+    hetero = hetero_leg(args, world, rank, dev, ctx, q3s, workloads, shard, np, torch, oracle,
+                        peak, max_over_ranks, gather)
+
+    results = {"hetero_decode_step": hetero}
     cpu = None
+    exact = None
     if rank == 0 and world == 1 and not args.no_secondary:
-        results = secondary(ctx, dev, q3s, workloads, np, torch)
-        oracle = oracle_mod()
+        results.update(secondary(ctx, dev, q3s, workloads, np, torch))
+        exact = exactness_counts(dev, q3s, workloads, np, torch, oracle)
         sample_rows = 16384
-        x = w.logits[:sample_rows].cpu().numpy()
+        wb = workloads.bandwidth(dev, rows=sample_rows, top_k=TOP_K, seed=3)
+        x = wb.logits.cpu().numpy()
         threads = cpu_threads()
-        rate, n = cpu_rows_per_s(oracle, x, VOCAB, q3s.make_params(1, top_k=TOP_K), 10.0,
-                                 threads)
+        p1 = q3s.make_params(1, top_k=TOP_K)
+        rate, n = cpu_rows_per_s(oracle, x, VOCAB, p1, 10.0, threads)
+        rate1, n1 = cpu_rows_per_s(oracle, x, VOCAB, p1, 5.0, 1)
         cpu = {"value": rate, "unit": "rows/s", "cores": threads, "kind": "port",
                "sample": f"{n} rows of the bandwidth workload (k=50), CPU restatement of "
-                         f"src/talker/sampling.rs with glibc expf, {threads} threads"}
+                         f"src/talker/sampling.rs with glibc expf, {threads} threads",
+               "single_thread": {"value": rate1, "unit": "rows/s", "cores": 1,
+                                 "sample": f"{n1} rows, 1 thread (the reference samples one "
+                                           f"row at a time on one thread)"}}
 
+    if not all(parity):
+        raise RuntimeError(f"parity failed on ranks {[i for i, p in enumerate(parity) if not p]}")
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
@@ -375,6 +474,9 @@ def main() -> int:
             "e2e": e2e,
             "gpu_launches": args.steps,
             "clocks": clocks.summary(),
+            "per_rank": per_rank,
+            "parity_rows_checked_per_rank": int(sel.size),
+            "exactness": exact,
             "results": results,
         }
         print(json.dumps(line), flush=True)
@@ -383,52 +485,120 @@ def main() -> int:
     return 0
 
 
-def secondary(ctx, dev, q3s, workloads, np, torch):
-    """Other configurations, device-resident, timed with CUDA events."""
-    out = {}
+def hetero_leg(args, world, rank, dev, ctx, q3s, workloads, shard, np, torch, oracle, peak,
+               max_over_ranks, gather):
+    """The heterogeneous full decode step: 4096 streams x (1 talker row of
+    3072 + 15 code-predictor rows of 2048), whole streams sharded over the
+    ranks; L2 flushed between launches.  Every rank checks a row sample of
+    its shard against the oracle."""
+    w = workloads.hetero(dev, streams=HETERO_STREAMS)
+    r0, r1 = shard.stream_range(HETERO_STREAMS, 16, world, rank)
+    a = w.device_args(dev)
+    R = r1 - r0
+    hoff = a["history_offsets"]
+    launch = q3s.prepare_batch(
+        w.logits, a["params"][r0 * 48:r1 * 48], a["seeds"][r0:r1], a["subseqs"][r0:r1],
+        row_offsets=a["row_offsets"][r0:r1], row_vocab=a["row_vocab"][r0:r1], vocab=a["vocab"],
+        history=a["history"], history_offsets=hoff[r0:r1 + 1], ctx=ctx)
+    sh = torch.cuda.current_stream(dev).cuda_stream
+    flush = L2Flush(torch, dev)
+    ms = time_each(torch, lambda: launch(sh), args.hetero_steps, flush)
+    ms_max = max_over_ranks(ms)
+    rows = np.arange(r0, r1)
+    H = (w.history_offsets[r0 + 1:r1 + 1] - w.history_offsets[r0:r1]).astype(np.int64)
+    V = w.row_vocab[r0:r1].astype(np.int64)
+    # logits + history ids + params (48) + seed + subseq + history offset +
+    # row offset (8 each) + row vocabulary (4) + token and status (5).
+    my_bytes = int((4 * V + 2 * H).sum()) + R * (48 + 8 + 8 + 8 + 8 + 4 + 5)
+    sel = np.sort(np.random.default_rng(200 + rank).choice(R, min(R, 512), replace=False))
+    ref = oracle.sample_rows(*w.oracle_layout(rows[sel]), nthreads=max(1, os.cpu_count() // world))
+    ok = bool(np.array_equal(launch.status.cpu().numpy()[sel], ref["status"]) and
+              np.array_equal(launch.tokens.cpu().numpy().view(np.uint32)[sel], ref["tokens"]))
+    per = gather({"rank": rank, "rows": R, "ms": ms, "bytes": my_bytes, "parity_ok": ok})
+    if not all(p["parity_ok"] for p in per):
+        raise RuntimeError(f"hetero parity failed: {per}")
+    total_rows = sum(p["rows"] for p in per)
+    gbs = [p["bytes"] / (p["ms"] / 1e3) / 1e9 for p in per]
+    del w, launch, flush
+    torch.cuda.empty_cache()
+    return {"streams": HETERO_STREAMS, "rows_total": total_rows, "n_gpus": world,
+            "rows_per_s": total_rows / (ms_max / 1e3), "ms_per_launch_max": ms_max,
+            "gbs_per_gpu": gbs, "hbm_frac_per_gpu": [g / peak for g in gbs],
+            "l2": "flushed between launches", "parity_rows_checked_per_rank": int(sel.size),
+            "per_rank": per}
 
-    def time_launches(fn, iters):
-        for _ in range(3):
-            fn()
+
+def exactness_counts(dev, q3s, workloads, np, torch, oracle):
+    """Tokens and statuses of every row of the five configurations against
+    the oracle with glibc expf (the reference's f32::exp on Linux): rows,
+    rows within 1e-6 of a CDF boundary, and mismatching rows."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import exactness
+    out = {}
+    cases = [("talker_single_1000", lambda: workloads.talker_single(dev, steps=1000)),
+             ("cp_frame_64x15", lambda: workloads.cp_frame(dev)),
+             ("talker_batch_1024", lambda: workloads.talker_batch(dev, rows=1024)),
+             ("bandwidth_65536_k1", lambda: workloads.bandwidth(dev, rows=65536, top_k=1)),
+             ("bandwidth_65536_k50", lambda: workloads.bandwidth(dev, rows=65536, top_k=50)),
+             ("bandwidth_65536_k256", lambda: workloads.bandwidth(dev, rows=65536, top_k=256)),
+             ("hetero_4096x16", lambda: workloads.hetero(dev, streams=4096))]
+    for name, make in cases:
+        w = make()
+        a = w.device_args(dev)
+        t, s = q3s.sample_batch(w.logits, a.pop("params"), a.pop("seeds"), a.pop("subseqs"), **a)
         torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(iters):
-            fn()
-        e1.record()
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / iters
+        rep = exactness.libm_report(w.oracle_layout(), t.cpu().numpy(), s.cpu().numpy(),
+                                    nthreads=cpu_threads())
+        out[name] = {k: rep[k] for k in ("rows", "boundary_rows", "draw_boundary_rows",
+                                         "topp_boundary_rows", "libm_mismatch_rows",
+                                         "status_mismatch_rows", "violations")}
+        del w, t, s
+    torch.cuda.empty_cache()
+    return out
+
+
+def secondary(ctx, dev, q3s, workloads, np, torch):
+    """Other configurations, device-resident, timed with CUDA events around
+    each launch; inputs smaller than L2 are flushed from it before each."""
+    out = {}
+    flush = L2Flush(torch, dev)
+    sh = torch.cuda.current_stream(dev).cuda_stream
 
     # B=1024 talker batch (penalty over histories, suppression, top-p 0.8).
     wb = workloads.talker_batch(dev, rows=1024)
     ab = wb.device_args(dev)
-    pb, sb, ub = ab.pop("params"), ab.pop("seeds"), ab.pop("subseqs")
-    ms = time_launches(lambda: q3s.sample_batch(wb.logits, pb, sb, ub, ctx=ctx, **ab), 50)
+    lb = q3s.prepare_batch(wb.logits, ab.pop("params"), ab.pop("seeds"), ab.pop("subseqs"),
+                           ctx=ctx, **ab)
+    ms = time_each(torch, lambda: lb(sh), 50, flush)
     hist_bytes = int(wb.history_offsets[-1]) * 2
     out["talker_batch_1024"] = {
-        "rows_per_s": 1024 / (ms / 1e3), "ms_per_launch": ms,
+        "rows_per_s": 1024 / (ms / 1e3), "ms_per_launch": ms, "l2": "flushed",
         "gbs": (1024 * (4 * 3072 + 16 + 8 + 5) + hist_bytes) / (ms / 1e3) / 1e9}
     for k in (1, 256):
         wk = workloads.bandwidth(dev, rows=65536, top_k=k, seed=9)
         ak = wk.device_args(dev)
-        pk, sk, uk = ak.pop("params"), ak.pop("seeds"), ak.pop("subseqs")
-        ms = time_launches(lambda: q3s.sample_batch(wk.logits, pk, sk, uk, ctx=ctx), 50)
+        lk = q3s.prepare_batch(wk.logits, ak.pop("params"), ak.pop("seeds"), ak.pop("subseqs"),
+                               ctx=ctx)
+        ms = time_each(torch, lambda: lk(sh), 50)
         out[f"bandwidth_k{k}"] = {"rows_per_s": 65536 / (ms / 1e3), "ms_per_launch": ms,
                                   "gbs": 65536 * BYTES_PER_ROW / (ms / 1e3) / 1e9}
-        del wk
+        del wk, lk
     # Code-predictor frame: 15 dependent bf16 [64, 2048] launches.
     wc = workloads.cp_frame(dev)
     ac = wc.device_args(dev)
     pc = ac.pop("params")
     sc, uc = ac.pop("seeds"), ac.pop("subseqs")
     x = wc.logits.view(15, 64, 2048)
+    groups = [q3s.prepare_batch(x[g], pc, sc[g * 64:(g + 1) * 64], uc[g * 64:(g + 1) * 64],
+                                ctx=ctx) for g in range(15)]
 
     def frame():
         for g in range(15):
-            q3s.sample_batch(x[g], pc, sc[g * 64:(g + 1) * 64], uc[g * 64:(g + 1) * 64], ctx=ctx)
-    ms = time_launches(frame, 20)
-    out["cp_frame_64x15"] = {"us_per_group": ms * 1e3 / 15, "rows_per_s": 960 / (ms / 1e3)}
+            groups[g](sh)
+    ms = time_each(torch, frame, 20, flush)
+    kms = time_each(torch, lambda: groups[0](sh), 50, flush)
+    out["cp_frame_64x15"] = {"us_per_group": ms * 1e3 / 15, "rows_per_s": 960 / (ms / 1e3),
+                             "kernel_us_one_group": kms * 1e3, "l2": "flushed per frame"}
     # Codebook embedding sum after sampling: 4096 streams, 16 codebooks
     # (3072 + 15 x 2048 ids), hidden 2048, bf16, a text row per stream.
     R, H = 4096, 2048
@@ -441,14 +611,16 @@ def secondary(ctx, dev, q3s, workloads, np, torch):
     text = torch.randn((R, H), device=dev, generator=g).to(torch.bfloat16)
     eout = (torch.empty((R, H), device=dev, dtype=torch.bfloat16),
             torch.empty(R, device=dev, dtype=torch.uint8))
-    ms = time_launches(lambda: q3s.embed_sum(codes, tables, text, ctx=ctx, out=eout), 50)
+    ebytes = R * (16 * H * 2 + H * 2 + H * 2 + 16 * 4 + 1)
+    res = {"tables_mb": sum(v * H * 2 for v in vocabs) / 1e6}
+    for label, fl in (("l2_flushed", flush), ("l2_warm", None)):
+        ms = time_each(torch, lambda: q3s.embed_sum(codes, tables, text, ctx=ctx, out=eout), 50,
+                       fl)
+        res[label] = {"us_per_launch": ms * 1e3, "rows_per_s": R / (ms / 1e3),
+                      "algorithmic_gbs": ebytes / (ms / 1e3) / 1e9}
     if not bool((eout[1] == 0).all()):
         raise RuntimeError("embedding sum failed")
-    ebytes = R * (16 * H * 2 + H * 2 + H * 2 + 16 * 4 + 1)
-    out["embed_sum_4096x16_h2048_bf16"] = {"us_per_launch": ms * 1e3,
-                                           "rows_per_s": R / (ms / 1e3),
-                                           "gbs": ebytes / (ms / 1e3) / 1e9,
-                                           "tables_mb": sum(v * H * 2 for v in vocabs) / 1e6}
+    out["embed_sum_4096x16_h2048_bf16"] = res
     del tables, text, eout
     # Single-stream talker step through the stateful Sampler (host round trip).
     ws = workloads.talker_single(dev, steps=200)
@@ -462,9 +634,16 @@ def secondary(ctx, dev, q3s, workloads, np, torch):
     for i in range(200):
         s.sample_with_mode(ws.logits[i], o, True, 2048, 2150, hist)
     dt = time.perf_counter() - t0
+    aw = ws.device_args(dev)
+    one = q3s.prepare_batch(ws.logits[0:1], aw["params"], aw["seeds"][:1], aw["subseqs"][:1],
+                            history=aw["history"], history_offsets=aw["history_offsets"][:2],
+                            ctx=ctx)
+    kms = time_each(torch, lambda: one(sh), 50, flush)
     out["talker_single_step"] = {"us_per_step": dt * 1e6 / 200,
+                                 "kernel_us": kms * 1e3,
                                  "note": "stateful Sampler call incl. H2D params/history and "
-                                         "D2H token+status, host wall clock"}
+                                         "D2H token+status, host wall clock; kernel_us is the "
+                                         "1-row launch alone (CUDA events, L2 flushed)"}
     return out
 
 

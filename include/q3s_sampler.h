@@ -164,6 +164,17 @@ void q3s_context_destroy(q3s_context* ctx);
  * caller advances subseq for rows whose status is OK and do_sample is set. */
 int q3s_sample_batch(q3s_context* ctx, const q3s_batch* batch, void* stream);
 
+/* Testing hook, no counterpart in the reference.  Every wait of the sampling
+ * kernel is bounded: a row whose staged logits do not arrive in time ends
+ * with Q3S_STATUS_NOT_RUN (the rows after it in its block too) and the call
+ * returns, so a stuck copy never hangs the device.  This sets, for the
+ * batched launches of `ctx`, the per-row wait limit (stage_wait_ns; 0 keeps
+ * the default of one second) and, with hold_refill != 0, stops the kernel
+ * from refilling a ring stage after its first row, so that every later row's
+ * wait runs out without any copy in flight.  Tests use it to exercise the
+ * give-up path; production code never calls it. */
+int q3s_context_set_test_hooks(q3s_context* ctx, uint64_t stage_wait_ns, int32_t hold_refill);
+
 /* Bytes of the file-scope device workspace of q3s_sample_batch_static, held on
  * every device that loads the library until the process exits. */
 #define Q3S_STATIC_SCRATCH_BYTES (32u * 1024u * 1024u)
@@ -180,9 +191,10 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* batch, void* stream);
  * q3s_sample_batch; in addition it rejects vocab > Q3S_MAX_VOCAB with
  * Q3S_E_INVALID_ARGUMENT, and it launches only as many blocks as the array
  * holds workspace for (about 14 bytes per vocabulary entry per warp, up to
- * 16 warps a block: 73 blocks at vocab 2048, 48 at 3072, 45 at 4096).  The first call on
- * a device looks up the array's address (cudaGetSymbolAddress, which may load
- * the module): make it before any stream capture.  Calls share the array and
+ * 16 warps a block: 73 blocks at vocab 2048, 48 at 3072, 45 at 4096).  Every
+ * call looks up the array's address on its device (cudaGetSymbolAddress,
+ * which allocates nothing); the first call on a device may load the module,
+ * so make it before any stream capture.  Calls share the array and
  * nothing in it has to start at zero; calls whose kernels overlap on the GPU
  * race on it, so order them on one stream or with events. */
 int q3s_sample_batch_static(q3s_context* ctx, const q3s_batch* batch, void* stream);

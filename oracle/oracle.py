@@ -47,7 +47,8 @@ class _Trace(ctypes.Structure):
     _fields_ = [("after_penalty", ctypes.c_void_p), ("after_temperature", ctypes.c_void_p),
                 ("final_probs", ctypes.c_void_p), ("masks", ctypes.c_void_p),
                 ("topk_threshold", ctypes.c_float), ("draw_threshold", ctypes.c_float),
-                ("draw_sum", ctypes.c_float), ("boundary_gap", ctypes.c_double)]
+                ("draw_sum", ctypes.c_float), ("boundary_gap", ctypes.c_double),
+                ("topp_gap", ctypes.c_double)]
 
 
 class _Sampler(ctypes.Structure):
@@ -103,12 +104,12 @@ def lib():
             ctypes.POINTER(_Sampler), ctypes.c_void_p, ctypes.c_size_t, _Options, ctypes.c_int,
             ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
             ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(_Trace)]
-        L.q3o_sample_rows.restype = ctypes.c_int
-        L.q3o_sample_rows.argtypes = [
+        L.q3o_sample_rows_ex.restype = ctypes.c_int
+        L.q3o_sample_rows_ex.argtypes = [
             ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
             ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
             ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-            ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int]
+            ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
         _lib = L
     return _lib
 
@@ -165,6 +166,7 @@ class SampleResult:
     draw_threshold: float
     draw_sum: float
     boundary_gap: float
+    topp_gap: float
 
 
 def sample_logits(logits, options, suppress_from=None, allow_token=None, history=(),
@@ -178,14 +180,14 @@ def sample_logits(logits, options, suppress_from=None, allow_token=None, history
     fp = np.zeros(n, np.float32)
     mk = np.zeros(n, np.uint8)
     tr = _Trace(_ptr(ap).value, _ptr(at).value, _ptr(fp).value, _ptr(mk).value, 0.0, 0.0, 0.0,
-                float("inf"))
+                float("inf"), float("inf"))
     tok = ctypes.c_uint32(0)
     drew = ctypes.c_int(0)
     st = lib().q3o_sample_logits(_ptr(x), n, _opt(options), _none(suppress_from),
                                  _none(allow_token), _ptr(h), h.size, float(uniform), exp_mode,
                                  ctypes.byref(tok), ctypes.byref(drew), ctypes.byref(tr))
     return SampleResult(st, tok.value, bool(drew.value), ap, at, fp, mk, tr.topk_threshold,
-                        tr.draw_threshold, tr.draw_sum, tr.boundary_gap)
+                        tr.draw_threshold, tr.draw_sum, tr.boundary_gap, tr.topp_gap)
 
 
 def greedy_select(logits, suppress_from=None, allow_token=None):
@@ -263,14 +265,16 @@ def sample_rows(logits: np.ndarray, offsets: np.ndarray, vocab: np.ndarray, para
     tokens = np.zeros(R, np.uint32)
     status = np.zeros(R, np.uint8)
     gap = np.zeros(R, np.float64)
+    tgap = np.zeros(R, np.float64)
     stride = int(vocab.max()) if (want_probs and R) else 0
     probs = np.zeros(R * stride, np.float32) if want_probs else None
     masks = np.zeros(R * stride, np.uint8) if want_probs else None
-    lib().q3o_sample_rows(_ptr(logits), R, _ptr(offsets), _ptr(vocab), _ptr(params), pstride,
-                          _ptr(seeds), _ptr(subseqs), _ptr(history), _ptr(history_offsets),
-                          _ptr(uo), exp_mode, _ptr(tokens), _ptr(status), _ptr(probs),
-                          _ptr(masks), stride, _ptr(gap), int(nthreads))
-    out = {"tokens": tokens, "status": status, "boundary_gap": gap}
+    lib().q3o_sample_rows_ex(_ptr(logits), R, _ptr(offsets), _ptr(vocab), _ptr(params),
+                             pstride, _ptr(seeds), _ptr(subseqs), _ptr(history),
+                             _ptr(history_offsets), _ptr(uo), exp_mode, _ptr(tokens),
+                             _ptr(status), _ptr(probs), _ptr(masks), stride, _ptr(gap),
+                             _ptr(tgap), int(nthreads))
+    out = {"tokens": tokens, "status": status, "boundary_gap": gap, "topp_gap": tgap}
     if want_probs:
         out["probs"] = probs.reshape(R, stride)
         out["masks"] = masks.reshape(R, stride)

@@ -271,10 +271,13 @@ extern "C" int q3o_sample_logits(const float* logits, size_t n, q3o_options opt,
     });
     float cumulative = 0.0f;
     const float top_p = (float)opt.top_p;
+    double gap = INFINITY;
     for (size_t pos = 0; pos < probs.size(); ++pos) {
+      if (pos > 0) gap = std::min(gap, fabs((double)cumulative - (double)top_p));
       if (pos > 0 && cumulative >= top_p) pen[probs[pos].idx] = -INFINITY;
       cumulative = cumulative + probs[pos].v;
     }
+    if (trace) trace->topp_gap = gap;
   }
   if (trace && trace->masks)
     for (size_t i = 0; i < n; ++i)
@@ -427,6 +430,7 @@ struct RowsJob {
   uint8_t* masks;
   int64_t probs_stride;
   double* boundary_gap;
+  double* topp_gap;
   int64_t begin, end;
 };
 
@@ -444,6 +448,7 @@ void run_rows(const RowsJob* j) {
     if (tr.final_probs) memset(tr.final_probs, 0, n * sizeof(float));
     if (tr.masks) memset(tr.masks, 0, n);
     tr.boundary_gap = INFINITY;
+    tr.topp_gap = INFINITY;
     uint32_t tok = 0;
     int st;
     if (!isfinite(p->repetition_penalty) || p->repetition_penalty <= 0.0) {
@@ -467,6 +472,7 @@ void run_rows(const RowsJob* j) {
     j->tokens[r] = st == Q3O_OK ? tok : 0u;
     j->status[r] = (uint8_t)st;
     if (j->boundary_gap) j->boundary_gap[r] = tr.boundary_gap;
+    if (j->topp_gap) j->topp_gap[r] = tr.topp_gap;
   }
 }
 
@@ -477,13 +483,14 @@ void* rows_thread(void* arg) {
 
 }  // namespace
 
-extern "C" int q3o_sample_rows(const float* logits, int64_t num_rows, const int64_t* offsets,
-                               const int32_t* vocab, const q3o_row_params* params,
-                               int64_t params_stride, const uint64_t* seeds,
-                               const uint64_t* subseqs, const uint16_t* hist, const int64_t* hoff,
-                               const float* uniform_override, int exp_mode, uint32_t* tokens,
-                               uint8_t* status, float* probs, uint8_t* masks,
-                               int64_t probs_stride, double* boundary_gap, int nthreads) {
+extern "C" int q3o_sample_rows_ex(const float* logits, int64_t num_rows, const int64_t* offsets,
+                                  const int32_t* vocab, const q3o_row_params* params,
+                                  int64_t params_stride, const uint64_t* seeds,
+                                  const uint64_t* subseqs, const uint16_t* hist,
+                                  const int64_t* hoff, const float* uniform_override, int exp_mode,
+                                  uint32_t* tokens, uint8_t* status, float* probs, uint8_t* masks,
+                                  int64_t probs_stride, double* boundary_gap, double* topp_gap,
+                                  int nthreads) {
   if (nthreads < 1) nthreads = 1;
   if (nthreads > num_rows) nthreads = (int)(num_rows > 0 ? num_rows : 1);
   std::vector<RowsJob> jobs(nthreads);
@@ -507,6 +514,7 @@ extern "C" int q3o_sample_rows(const float* logits, int64_t num_rows, const int6
     j.masks = masks;
     j.probs_stride = probs_stride;
     j.boundary_gap = boundary_gap;
+    j.topp_gap = topp_gap;
     j.begin = num_rows * t / nthreads;
     j.end = num_rows * (t + 1) / nthreads;
   }
@@ -517,4 +525,16 @@ extern "C" int q3o_sample_rows(const float* logits, int64_t num_rows, const int6
   for (int t = 0; t < nthreads; ++t) pthread_create(&tids[t], nullptr, rows_thread, &jobs[t]);
   for (int t = 0; t < nthreads; ++t) pthread_join(tids[t], nullptr);
   return 0;
+}
+
+extern "C" int q3o_sample_rows(const float* logits, int64_t num_rows, const int64_t* offsets,
+                               const int32_t* vocab, const q3o_row_params* params,
+                               int64_t params_stride, const uint64_t* seeds,
+                               const uint64_t* subseqs, const uint16_t* hist, const int64_t* hoff,
+                               const float* uniform_override, int exp_mode, uint32_t* tokens,
+                               uint8_t* status, float* probs, uint8_t* masks,
+                               int64_t probs_stride, double* boundary_gap, int nthreads) {
+  return q3o_sample_rows_ex(logits, num_rows, offsets, vocab, params, params_stride, seeds,
+                            subseqs, hist, hoff, uniform_override, exp_mode, tokens, status,
+                            probs, masks, probs_stride, boundary_gap, nullptr, nthreads);
 }

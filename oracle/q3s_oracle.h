@@ -56,6 +56,8 @@ typedef struct q3o_trace {
   float draw_threshold;   /* (r as f32) * sum */
   float draw_sum;         /* the sequential f32 softmax sum */
   double boundary_gap;    /* min |cum_j - threshold| / sum over the crossing neighbours */
+  double topp_gap;        /* min over the nucleus decisions (positions >= 1) of
+                             |cumulative before the position - top_p|; +inf without top-p */
 } q3o_trace;
 
 typedef struct q3o_sampler { /* Sampler state, sampling.rs:144-155 */
@@ -122,6 +124,16 @@ int q3o_sample_rows(const float* logits, int64_t num_rows, const int64_t* offset
                     const int64_t* hoff, const float* uniform_override, int exp_mode,
                     uint32_t* tokens, uint8_t* status, float* probs, uint8_t* masks,
                     int64_t probs_stride, double* boundary_gap, int nthreads);
+
+/* q3o_sample_rows plus the per-row top-p decision gap (q3o_trace.topp_gap);
+ * topp_gap may be NULL. */
+int q3o_sample_rows_ex(const float* logits, int64_t num_rows, const int64_t* offsets,
+                       const int32_t* vocab, const q3o_row_params* params, int64_t params_stride,
+                       const uint64_t* seeds, const uint64_t* subseqs, const uint16_t* hist,
+                       const int64_t* hoff, const float* uniform_override, int exp_mode,
+                       uint32_t* tokens, uint8_t* status, float* probs, uint8_t* masks,
+                       int64_t probs_stride, double* boundary_gap, double* topp_gap,
+                       int nthreads);
 
 #ifdef __cplusplus
 }

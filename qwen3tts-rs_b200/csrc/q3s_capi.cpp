@@ -6,6 +6,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include <cuda_runtime.h>
 
@@ -65,9 +66,19 @@ struct q3s_context {
   size_t hist_cap = 0;
   unsigned* h_out = nullptr;  // pinned: token, status byte in the next word
   unsigned* d_out = nullptr;
-  // General-path workspace of the sampling kernel (grown on demand).
-  unsigned char* scratch = nullptr;
-  size_t scratch_bytes = 0;
+  // General-path workspaces of the sampling kernel, one per stream that has
+  // launched through this context (grown on demand), so launches on
+  // different streams never share one.
+  struct Workspace {
+    cudaStream_t stream;
+    unsigned char* ptr;
+    size_t bytes;
+  };
+  std::mutex ws_mu;
+  std::vector<Workspace> ws;
+  // Testing hooks (q3s_context_set_test_hooks).
+  uint64_t test_wait_ns = 0;
+  int test_hold_refill = 0;
 };
 
 struct q3s_sampler {
@@ -159,7 +170,8 @@ void q3s_context_destroy(q3s_context* c) {
     if (c->d_hist) cudaFree(c->d_hist);
     if (c->h_out) cudaFreeHost(c->h_out);
     if (c->d_out) cudaFree(c->d_out);
-    if (c->scratch) cudaFree(c->scratch);
+    for (auto& w : c->ws)
+      if (w.ptr) cudaFree(w.ptr);
   }
   delete c;
 }
@@ -205,6 +217,8 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* b, void* stream) {
   a.probs = b->probs;
   a.masks = b->masks;
   a.probs_stride = b->probs_stride;
+  if (ctx->test_wait_ns) a.wait_ns = ctx->test_wait_ns;
+  a.hold_refill = ctx->test_hold_refill;
   int cap = b->vocab < Q3S_MAX_VOCAB ? b->vocab : Q3S_MAX_VOCAB;
   a.vcap = ((cap > 0 ? cap : 1) + 31) / 32 * 32;
   const int warps = q3s::sample_max_warps(a.vcap, b->dtype, ctx->smem_optin);
@@ -213,18 +227,38 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* b, void* stream) {
   if (blocks > ctx->sm_count) blocks = ctx->sm_count;
   const size_t need = (size_t)blocks * warps * q3s::sample_scratch_per_warp(a.vcap);
   cudaError_t e;
-  if (need > ctx->scratch_bytes) {
-    // Launches on one context are stream-ordered users of this workspace.
-    if (ctx->scratch) cudaFree(ctx->scratch);
-    ctx->scratch = nullptr;
-    ctx->scratch_bytes = 0;
-    if ((e = cudaMalloc((void**)&ctx->scratch, need)) != cudaSuccess)
-      return cuda_fail(e, "cudaMalloc(sampler workspace)");
-    ctx->scratch_bytes = need;
+  {
+    // The stream's own workspace: launches on one stream are ordered, so
+    // they may share it; another stream gets another one.
+    std::lock_guard<std::mutex> lock(ctx->ws_mu);
+    const cudaStream_t key = (cudaStream_t)stream;
+    q3s_context::Workspace* w = nullptr;
+    for (auto& x : ctx->ws)
+      if (x.stream == key) w = &x;
+    if (!w) {
+      ctx->ws.push_back(q3s_context::Workspace{key, nullptr, 0});
+      w = &ctx->ws.back();
+    }
+    if (need > w->bytes) {
+      // cudaFree waits for the device, so no launch still uses the old one.
+      if (w->ptr) cudaFree(w->ptr);
+      w->ptr = nullptr;
+      w->bytes = 0;
+      if ((e = cudaMalloc((void**)&w->ptr, need)) != cudaSuccess)
+        return cuda_fail(e, "cudaMalloc(sampler workspace)");
+      w->bytes = need;
+    }
+    a.scratch = w->ptr;
   }
-  a.scratch = ctx->scratch;
   e = q3s::launch_sample(a, (int)blocks, warps, (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "sample kernel launch");
+  return Q3S_OK;
+}
+
+int q3s_context_set_test_hooks(q3s_context* ctx, uint64_t stage_wait_ns, int32_t hold_refill) {
+  if (!ctx) return fail(Q3S_E_INVALID_ARGUMENT, "q3s_context_set_test_hooks: NULL context");
+  ctx->test_wait_ns = stage_wait_ns;
+  ctx->test_hold_refill = hold_refill ? 1 : 0;
   return Q3S_OK;
 }
 

@@ -33,6 +33,11 @@ struct KernelArgs {
   long long probs_stride;
   int vcap;  // per-warp row capacity in elements (multiple of 32)
   unsigned char* scratch;  // general-path workspace: sample_scratch_per_warp(vcap) per warp
+  // Limit of each per-row stage wait (the end-of-block drain keeps its own
+  // one-second limit).  Testing hook: hold_refill stops the ring refills, so
+  // every row after a stage's first one waits for a generation nothing issues.
+  unsigned long long wait_ns = 1000000000ull;
+  int hold_refill = 0;
 };
 
 size_t sample_smem_per_warp(int vcap, int dtype);

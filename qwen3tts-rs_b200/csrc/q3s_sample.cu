@@ -38,6 +38,7 @@
 // same algorithm warp-cooperatively on full-row lists kept in a per-warp
 // global workspace ("general path").
 
+#include <atomic>
 #include <cstdint>
 
 #include "../../include/q3s_sampler.h"
@@ -804,7 +805,7 @@ __device__ __forceinline__ void release(Releaser& r) {
   if (r.done) return;
   r.done = true;
   __syncwarp();
-  if (lane_id() == 0 && r.next < r.a->num_rows &&
+  if (lane_id() == 0 && r.next < r.a->num_rows && !r.a->hold_refill &&
       *reinterpret_cast<volatile uint32_t*>(&r.ctl->abort) == 0u) {
     fence_proxy_async_smem();
     issue_row<DT>(*r.a, r.next, r.stage, &r.ctl->full[r.slot]);
@@ -815,8 +816,9 @@ __device__ __forceinline__ void release(Releaser& r) {
 
 // Waits for generation `gen` of stage `slot`: first until it has been issued
 // (a later generation's parity must not be tested against an earlier
-// phase), then for its bytes.  False when a wait gave up or the block aborts.
-__device__ bool wait_stage(RingCtl* ctl, int slot, uint32_t gen) {
+// phase), then for its bytes.  False when a wait gave up (after limit_ns) or
+// the block aborts.
+__device__ bool wait_stage(RingCtl* ctl, int slot, uint32_t gen, uint64_t limit_ns) {
   if (*reinterpret_cast<volatile uint32_t*>(&ctl->abort) != 0u) return false;
   uint64_t t0;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
@@ -825,10 +827,10 @@ __device__ bool wait_stage(RingCtl* ctl, int slot, uint32_t gen) {
     __nanosleep(128);
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    if (t - t0 > WAIT_LIMIT_NS) return false;
+    if (t - t0 > limit_ns) return false;
   }
   __threadfence_block();
-  return mbar_wait_bounded(&ctl->full[slot], gen & 1u, WAIT_LIMIT_NS);
+  return mbar_wait_bounded(&ctl->full[slot], gen & 1u, limit_ns);
 }
 
 // Vector maxima of the stage (registers) and the row maximum.  Lane l owns
@@ -1716,7 +1718,7 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
       }
       __syncwarp();
     }
-    const bool ready = wait_stage(ctl, slot, gen);
+    const bool ready = wait_stage(ctl, slot, gen, a.wait_ns);
     if (!__all_sync(FULL, ready)) {
       // A wait gave up (or the block aborts): this row is not run, no copy
       // is issued any more, and later tickets fail fast.
@@ -1799,11 +1801,32 @@ __global__ void greedy_kernel(const void* logits, long long num_rows, long long 
   }
 }
 
+constexpr int MAX_DEVICES = 64;
+
+// Raises a kernel's dynamic shared-memory limit on the current device to at
+// least `smem`, once per (kernel, device, size): the attribute call is not
+// repeated on every launch.
+template <typename K>
+cudaError_t ensure_smem(K kernel, std::atomic<int>* set, size_t smem) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::atomic<int>* slot = (dev >= 0 && dev < MAX_DEVICES) ? &set[dev] : nullptr;
+  if (slot && slot->load(std::memory_order_relaxed) >= (int)smem) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess && slot) {
+    int cur = slot->load(std::memory_order_relaxed);
+    while (cur < (int)smem && !slot->compare_exchange_weak(cur, (int)smem)) {
+    }
+  }
+  return e;
+}
+
 template <int DT, int NJ, bool DBG>
 cudaError_t launch_dbg(const KernelArgs& a, int grid, int warps, cudaStream_t stream) {
+  static std::atomic<int> smem_set[MAX_DEVICES];
   const size_t smem = block_smem(a.vcap, Elem<DT>::BYTES, warps);
-  cudaError_t e = cudaFuncSetAttribute(sample_kernel<DT, NJ, DBG>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = ensure_smem(sample_kernel<DT, NJ, DBG>, smem_set, smem);
   if (e != cudaSuccess) return e;
   sample_kernel<DT, NJ, DBG><<<grid, warps * 32, smem, stream>>>(a);
   return cudaGetLastError();

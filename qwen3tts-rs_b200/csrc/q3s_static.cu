@@ -8,15 +8,15 @@
 // q3s_sample_batch.
 //
 // The array is Q3S_STATIC_SCRATCH_BYTES (32 MiB) on every device that loads
-// the library, held until the process exits.  Its address is looked up once
-// per device, with that device current, by the first call on the device
-// (cudaGetSymbolAddress, which may load the module): make that first call
-// before any stream capture.  Every call on a device shares the array; the
+// the library, held until the process exits.  Every call looks its address
+// up with the call's device current (cudaGetSymbolAddress allocates nothing),
+// so the address stays right after a device reset re-creates the context and
+// reloads the module.  The first call on a device may load the module: make
+// that first call before any stream capture.  Every call on a device shares the array; the
 // kernel writes every workspace word of a row before reading it, so nothing
 // has to start at zero and nothing is cleared.  Calls whose kernels overlap
 // on the GPU (other streams, other host threads, other contexts of the same
 // device) race on the array: order them on one stream or with events.
-#include <mutex>
 #include <string>
 
 #include <cuda_runtime.h>
@@ -29,20 +29,14 @@ namespace {
 
 __device__ __align__(256) unsigned char g_static_scratch[Q3S_STATIC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_setup_mu;
-unsigned char* g_static_ptr[kMaxDevices];  // per device, written once under g_setup_mu
-
-// Device address of g_static_scratch on the current device (`device`).
-cudaError_t static_scratch(int device, unsigned char** out) {
-  std::lock_guard<std::mutex> lock(g_setup_mu);
-  if (!g_static_ptr[device]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
-    if (e != cudaSuccess) return e;
-    g_static_ptr[device] = static_cast<unsigned char*>(p);
-  }
-  *out = g_static_ptr[device];
+// Device address of g_static_scratch on the current device.  Host code only
+// holds a stand-in for the array, never its device address, so the address
+// is asked of the runtime for the current device on every call.
+cudaError_t static_scratch(unsigned char** out) {
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+  if (e != cudaSuccess) return e;
+  *out = static_cast<unsigned char*>(p);
   return cudaSuccess;
 }
 
@@ -89,13 +83,10 @@ extern "C" int q3s_sample_batch_static(q3s_context* ctx, const q3s_batch* b, voi
   if ((b->probs || b->masks) && b->probs_stride < b->vocab)
     return record_error(Q3S_E_INVALID_ARGUMENT, "probs_stride must be >= vocab");
   const q3s::ContextInfo ci = q3s::context_info(ctx);
-  if (ci.device < 0 || ci.device >= kMaxDevices)
-    return record_error(Q3S_E_INVALID_ARGUMENT,
-                        "q3s_sample_batch_static: device index beyond the static set-up table");
   CurrentDevice g(ci.device);
   if (g.err != cudaSuccess) return q3s::record_cuda_error(g.err, "cudaSetDevice");
   unsigned char* scratch = nullptr;
-  cudaError_t e = static_scratch(ci.device, &scratch);
+  cudaError_t e = static_scratch(&scratch);
   if (e != cudaSuccess) return q3s::record_cuda_error(e, "cudaGetSymbolAddress(static workspace)");
   q3s::KernelArgs a;
   a.logits = b->logits;

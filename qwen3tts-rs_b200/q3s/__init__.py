@@ -119,7 +119,7 @@ EXPORTED_SYMBOLS = (
     "q3s_sampler_destroy", "q3s_sampler_subsequence_counter",
     "q3s_sampler_set_subsequence_counter", "q3s_sampler_get_diagnostics",
     "q3s_sampler_sample_with_mode", "q3s_sampler_sample", "q3s_sample_batch_static",
-    "q3s_embed_sum",
+    "q3s_embed_sum", "q3s_context_set_test_hooks",
 )
 
 _lib = None
@@ -148,6 +148,7 @@ def load(path: Optional[os.PathLike] = None):
     L.q3s_context_create.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]
     L.q3s_context_destroy.argtypes = [ctypes.c_void_p]
     L.q3s_context_destroy.restype = None
+    L.q3s_context_set_test_hooks.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int32]
     L.q3s_sample_batch.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Batch), ctypes.c_void_p]
     L.q3s_sample_batch_static.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Batch),
                                           ctypes.c_void_p]
@@ -227,6 +228,14 @@ class Context:
     def handle(self) -> ctypes.c_void_p:
         return self._h
 
+    def set_test_hooks(self, stage_wait_ns: int = 0, hold_refill: bool = False) -> None:
+        """Testing hook (q3s_context_set_test_hooks): the per-row stage-wait
+        limit of this context's batched launches (0 = the default second) and
+        whether ring stages are refilled after their first row."""
+        _check(load().q3s_context_set_test_hooks(self._h, int(stage_wait_ns),
+                                                 1 if hold_refill else 0),
+               "q3s_context_set_test_hooks")
+
     def close(self) -> None:
         if self._h:
             load().q3s_context_destroy(self._h)
@@ -305,8 +314,58 @@ def sample_batch_static(logits, params, seeds=None, subseqs=None, *, row_offsets
                          out=out)
 
 
+class PreparedBatch:
+    """A q3s_batch built once and launched many times (each launch is one C
+    call: no argument marshalling per step).  Holds references to every
+    tensor it points at; `tokens` / `status` are its outputs."""
+
+    def __init__(self, entry: str, batch, ctx: "Context", keep: tuple, tokens, status):
+        self._fn = getattr(load(), entry)
+        self._entry = entry
+        self._b = batch
+        self._ref = ctypes.byref(batch)
+        self._ctx = ctx
+        self._keep = keep
+        self.tokens = tokens
+        self.status = status
+
+    def __call__(self, stream: int) -> None:
+        rc = self._fn(self._ctx.handle, self._ref, ctypes.c_void_p(stream))
+        if rc != OK:
+            _check(rc, self._entry)
+
+
+def prepare_batch(logits, params, seeds=None, subseqs=None, *, row_offsets=None,
+                  row_vocab=None, vocab: Optional[int] = None, history=None,
+                  history_offsets=None, ctx: Optional[Context] = None, out=None,
+                  static: bool = False) -> PreparedBatch:
+    """sample_batch's arguments fixed once; call the result with a stream
+    handle to launch (q3s_sample_batch, or q3s_sample_batch_static)."""
+    entry = "q3s_sample_batch_static" if static else "q3s_sample_batch"
+    b, ctx, keep, tokens, status = _build_batch(
+        logits, params, seeds, subseqs, row_offsets=row_offsets, row_vocab=row_vocab,
+        vocab=vocab, history=history, history_offsets=history_offsets, uniform_override=None,
+        debug=False, ctx=ctx, out=out)
+    return PreparedBatch(entry, b, ctx, keep, tokens, status)
+
+
 def _launch_batch(entry: str, logits, params, seeds, subseqs, *, row_offsets, row_vocab, vocab,
                   history, history_offsets, uniform_override, debug, ctx, stream, out):
+    import torch
+    b, ctx, keep, tokens, status = _build_batch(
+        logits, params, seeds, subseqs, row_offsets=row_offsets, row_vocab=row_vocab,
+        vocab=vocab, history=history, history_offsets=history_offsets,
+        uniform_override=uniform_override, debug=debug, ctx=ctx, out=out)
+    dev = logits.device
+    s = torch.cuda.current_stream(dev).cuda_stream if stream is None else stream
+    _check(getattr(load(), entry)(ctx.handle, ctypes.byref(b), ctypes.c_void_p(s)), entry)
+    if debug:
+        return tokens, status, keep[-2], keep[-1]
+    return tokens, status
+
+
+def _build_batch(logits, params, seeds, subseqs, *, row_offsets, row_vocab, vocab, history,
+                 history_offsets, uniform_override, debug, ctx, out):
     import torch
     dev = logits.device
     if logits.dtype == torch.float32:
@@ -363,11 +422,9 @@ def _launch_batch(entry: str, logits, params, seeds, subseqs, *, row_offsets, ro
     b.probs = _dptr(probs)
     b.masks = _dptr(masks)
     b.probs_stride = V if debug else 0
-    s = torch.cuda.current_stream(dev).cuda_stream if stream is None else stream
-    _check(getattr(load(), entry)(ctx.handle, ctypes.byref(b), ctypes.c_void_p(s)), entry)
-    if debug:
-        return tokens, status, probs, masks
-    return tokens, status
+    keep = (logits, params, seeds, subseqs, row_offsets, row_vocab, history, history_offsets,
+            uniform_override, probs, masks)
+    return b, ctx, keep, tokens, status
 
 
 def embed_sum(codes, tables, text=None, *, ctx: Optional[Context] = None, stream=None,
@@ -395,21 +452,30 @@ def embed_sum(codes, tables, text=None, *, ctx: Optional[Context] = None, stream
     else:
         raise TypeError("tables must be float32 or bfloat16")
     H = int(tables[0].shape[1])
+    dev = codes.device
+    # The C entry point has no sizes to check these against: a mismatch here
+    # would make the kernel read or write past a buffer.
     for t in tables:
         if t.dtype != dt or t.dim() != 2 or int(t.shape[1]) != H or t.stride(1) != 1:
             raise ValueError("tables must share dtype and width and have contiguous rows")
         if t.stride(0) != H:
             raise ValueError("tables must be contiguous")
-    dev = codes.device
+        if t.device != dev:
+            raise ValueError("every table must be on the codes' device")
     codes = codes.contiguous()
     stride = 0
     if text is not None:
         if text.dtype != dt:
             raise TypeError("text must have the tables' dtype")
+        if text.device != dev:
+            raise ValueError("text must be on the codes' device")
         if text.dim() == 1:
+            if int(text.shape[0]) != H or text.stride(0) != 1:
+                raise ValueError("a 1-D text must be one contiguous row of H elements")
             stride = 0
         else:
-            if text.shape[0] != R or text.stride(1) != 1:
+            if text.dim() != 2 or text.shape[0] != R or int(text.shape[1]) != H or \
+                    text.stride(1) != 1:
                 raise ValueError("text must be [H] or [R, H] with contiguous rows")
             stride = text.stride(0)
     ctx = ctx or default_context(dev.index)
@@ -418,6 +484,12 @@ def embed_sum(codes, tables, text=None, *, ctx: Optional[Context] = None, stream
         status = torch.empty(R, dtype=torch.uint8, device=dev)
     else:
         res, status = out
+        if tuple(res.shape) != (R, H) or res.dtype != dt or res.device != dev or \
+                not res.is_contiguous():
+            raise ValueError("out[0] must be a contiguous [R, H] tensor of the tables' dtype "
+                             "on the codes' device")
+        if tuple(status.shape) != (R,) or status.dtype != torch.uint8 or status.device != dev:
+            raise ValueError("out[1] must be a uint8 [R] tensor on the codes' device")
     ptrs = (ctypes.c_void_p * G)(*[t.data_ptr() for t in tables])
     vocab = (ctypes.c_int32 * G)(*[int(t.shape[0]) for t in tables])
     b = _EmbedBatch()

@@ -119,3 +119,25 @@ def test_rejects_bad_arguments():
         q3s.embed_sum(c, [t, t])
     with pytest.raises(ValueError):
         q3s.embed_sum(torch.zeros((2, 33), dtype=torch.int32, device=DEV), [t] * 33)
+    # Widths, shapes and devices the C entry point cannot check itself.
+    t2 = torch.zeros((4, 8), device=DEV)
+    c1 = torch.zeros((2, 1), dtype=torch.int32, device=DEV)
+    with pytest.raises(ValueError):
+        q3s.embed_sum(c1, [t2], torch.zeros(7, device=DEV))  # 1-D text of the wrong width
+    with pytest.raises(ValueError):
+        q3s.embed_sum(c1, [t2], torch.zeros((2, 9), device=DEV))  # [R, H'] text
+    with pytest.raises(ValueError):
+        q3s.embed_sum(c1, [t2], torch.zeros((3, 8), device=DEV))  # wrong number of rows
+    with pytest.raises(ValueError):
+        q3s.embed_sum(c1, [t2], torch.zeros(8))  # text on the host
+    with pytest.raises(ValueError):
+        q3s.embed_sum(c1, [t2.cpu()])  # table on the host
+    ok_out = (torch.empty((2, 8), device=DEV), torch.empty(2, dtype=torch.uint8, device=DEV))
+    q3s.embed_sum(c1, [t2], out=ok_out)
+    for bad in ((torch.empty((2, 9), device=DEV), ok_out[1]),
+                (torch.empty((2, 8), device=DEV, dtype=torch.bfloat16), ok_out[1]),
+                (torch.empty((2, 8)), ok_out[1]),
+                (ok_out[0], torch.empty(3, dtype=torch.uint8, device=DEV)),
+                (ok_out[0], torch.empty(2, dtype=torch.int32, device=DEV))):
+        with pytest.raises(ValueError):
+            q3s.embed_sum(c1, [t2], out=bad)

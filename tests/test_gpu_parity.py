@@ -422,3 +422,69 @@ def test_greedy_batch_modes_match_oracle():
             want = oracle.greedy_select_on_device(x, sf, allow)
             got = q3s.greedy_select_on_device(xt, sf, allow)
             assert int(got.item()) == want, (n, trial)
+
+
+# ---------------------------------------------------------------------------
+# Bounded waits and concurrent streams.
+# ---------------------------------------------------------------------------
+def oracle_tokens(w):
+    lay = w.oracle_layout()
+    return oracle.sample_rows(*lay, nthreads=oracle.cpu_count())
+
+
+def test_bounded_stage_wait_gives_up_and_context_stays_usable():
+    """With the ring refills held back, every row after a stage's first one
+    waits for a generation that is never issued (no copy is in flight): the
+    wait runs out after 2 ms, the row and the rest of its block end
+    NOT_RUN, and the call returns.  The same context then samples normally."""
+    R = 4096
+    w = workloads.bandwidth(DEV, rows=R, top_k=50)
+    ref = oracle_tokens(w)
+    ctx = q3s.Context(0)
+    a = w.device_args(DEV)
+    p, s, u = a.pop("params"), a.pop("seeds"), a.pop("subseqs")
+    ctx.set_test_hooks(stage_wait_ns=2_000_000, hold_refill=True)
+    t, st = q3s.sample_batch(w.logits, p, s, u, ctx=ctx)
+    torch.cuda.synchronize()
+    st = st.cpu().numpy()
+    t = t.cpu().numpy().view(np.uint32)
+    assert set(np.unique(st).tolist()) <= {q3s.STATUS_OK, 255}
+    grid = min((R + 15) // 16, torch.cuda.get_device_properties(DEV).multi_processor_count)
+    ticket = np.arange(R) // grid  # row = block + ticket * grid
+    assert np.all(st[ticket >= 8] == 255)  # every refill-dependent row gave up
+    ok = st == q3s.STATUS_OK
+    assert ok.sum() >= 1
+    np.testing.assert_array_equal(t[ok], ref["tokens"][ok])
+    ctx.set_test_hooks(0, False)
+    t2, st2 = q3s.sample_batch(w.logits, p, s, u, ctx=ctx)
+    torch.cuda.synchronize()
+    assert bool((st2 == 0).all())
+    np.testing.assert_array_equal(t2.cpu().numpy().view(np.uint32), ref["tokens"])
+
+
+def test_general_path_rows_on_two_streams_of_one_context():
+    """Rows on the general path (top-k off, top-p 0.8, penalties: the
+    1024-row talker batch) use the per-stream workspace; two streams of one
+    context run them concurrently and both match the oracle."""
+    ctx = q3s.Context(0)
+    ws = [workloads.talker_batch(DEV, rows=1024, seed=2),
+          workloads.talker_batch(DEV, rows=1024, seed=12)]
+    refs = [oracle_tokens(w) for w in ws]
+    streams = [torch.cuda.Stream(DEV), torch.cuda.Stream(DEV)]
+    args = []
+    for w in ws:
+        a = w.device_args(DEV)
+        args.append((a.pop("params"), a.pop("seeds"), a.pop("subseqs"), a))
+    torch.cuda.synchronize()
+    outs = [None, None]
+    for _ in range(6):
+        for i in range(2):
+            p, s, u, a = args[i]
+            with torch.cuda.stream(streams[i]):
+                outs[i] = q3s.sample_batch(ws[i].logits, p, s, u, ctx=ctx,
+                                           stream=streams[i].cuda_stream, **a)
+    torch.cuda.synchronize()
+    for i in range(2):
+        t, st = outs[i]
+        np.testing.assert_array_equal(st.cpu().numpy(), refs[i]["status"])
+        np.testing.assert_array_equal(t.cpu().numpy().view(np.uint32), refs[i]["tokens"])
