@@ -221,8 +221,13 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* b, void* stream) {
   a.hold_refill = ctx->test_hold_refill;
   int cap = b->vocab < Q3S_MAX_VOCAB ? b->vocab : Q3S_MAX_VOCAB;
   a.vcap = ((cap > 0 ? cap : 1) + 31) / 32 * 32;
-  const int warps = q3s::sample_max_warps(a.vcap, b->dtype, ctx->smem_optin);
+  int warps = q3s::sample_max_warps(a.vcap, b->dtype, ctx->smem_optin);
   if (warps < 1) return fail(Q3S_E_INVALID_ARGUMENT, "vocabulary does not fit shared memory");
+  // A batch that does not fill every SM with full blocks spreads its rows
+  // over all SMs with fewer warps per block: rows run in parallel rather
+  // than queueing on a few SMs.
+  if (b->num_rows < (long long)warps * ctx->sm_count)
+    warps = (int)((b->num_rows + ctx->sm_count - 1) / ctx->sm_count);
   long long blocks = (b->num_rows + warps - 1) / warps;
   if (blocks > ctx->sm_count) blocks = ctx->sm_count;
   const size_t need = (size_t)blocks * warps * q3s::sample_scratch_per_warp(a.vcap);

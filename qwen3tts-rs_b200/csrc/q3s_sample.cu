@@ -380,6 +380,47 @@ __device__ __forceinline__ bool load_plan(const RowPlan* slot, uint32_t ticket, 
   return w[7] == ticket;
 }
 
+// The history bitmap of a row (sampling.rs:732-773: every id < n of the
+// history marks its entry once): bm[0 .. ceil(n/32)) cleared, then one bit
+// per id.  The ids are read as 16-byte vectors of 8, four vectors per lane in
+// flight (1024 ids per round trip of the warp), plus the unaligned head and
+// tail one id per lane; vector slots past the end read as 0xFFFF, which no
+// row's vocabulary reaches.
+__device__ __forceinline__ void mark_id(uint32_t* bm, uint32_t id, int n) {
+  if ((int)id < n) atomicOr(&bm[id >> 5], 1u << (id & 31));
+}
+
+__device__ __noinline__ void fill_history(const unsigned short* h, long long cnt, int n,
+                                          uint32_t* bm) {
+  const int lane = (int)lane_id();
+  for (int w = lane; w < ((n + 31) >> 5); w += 32) bm[w] = 0u;
+  __syncwarp();
+  long long head = (long long)(((16u - (uint32_t)(reinterpret_cast<uintptr_t>(h) & 15u)) & 15u) >> 1);
+  if (head > cnt) head = cnt;
+  if (lane < head) mark_id(bm, __ldg(h + lane), n);
+  const uint4* v = reinterpret_cast<const uint4*>(h + head);
+  const long long nv = (cnt - head) >> 3;
+  for (long long q0 = 0; q0 < nv; q0 += 128) {
+    uint4 w[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const long long q = q0 + r * 32 + lane;
+      w[r] = q < nv ? __ldg(v + q) : make_uint4(~0u, ~0u, ~0u, ~0u);
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const uint32_t ws[4] = {w[r].x, w[r].y, w[r].z, w[r].w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        mark_id(bm, ws[t] & 0xFFFFu, n);
+        mark_id(bm, ws[t] >> 16, n);
+      }
+    }
+  }
+  for (long long t = head + nv * 8 + lane; t < cnt; t += 32) mark_id(bm, __ldg(h + t), n);
+  __syncwarp();
+}
+
 // Per-row transform inputs.
 struct RowCtx {
   int n, mis, Q;
@@ -466,78 +507,78 @@ __device__ K warp_select(int n, uint32_t k, KeyFn keyfn, uint32_t* hist, int top
   return prefix;
 }
 
-// Ascending bitonic sort of 256 keys held 8 per lane (element lane*8 + r).
-__device__ inline void bitonic_sort_256(unsigned long long (&v)[8]) {
-  const unsigned lane = lane_id();
-#pragma unroll
-  for (int size = 2; size <= 256; size <<= 1) {
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      if (stride >= 8) {
-        const int ls = stride >> 3;
-        const bool lower = (lane & ls) == 0;
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          const bool up = (((int)lane * 8 + r) & size) == 0;
-          const unsigned long long o = __shfl_xor_sync(FULL, v[r], ls);
-          const bool keep_min = (lower == up);
-          v[r] = keep_min ? (o < v[r] ? o : v[r]) : (o > v[r] ? o : v[r]);
-        }
-      } else {
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          if ((r & stride) == 0) {
-            const bool up = (((int)lane * 8 + r) & size) == 0;
-            const unsigned long long a = v[r], b = v[r + stride];
-            if ((a > b) == up) {
-              v[r] = b;
-              v[r + stride] = a;
-            }
-          }
-        }
-      }
-    }
-  }
-}
+template <int R, typename T>
+__device__ __forceinline__ void bitonic(T (&v)[R]);
 
-// Sequential f32 sum of B[0..count) by lane 0, in order; when `prefix` is set
-// B[j] is replaced by the running sum.  Result broadcast to every lane.
-// B is 16-byte aligned; four terms are loaded at a time, added in order.
-__device__ inline float chain_sum(float* B, int count, bool prefix) {
+// Ascending bitonic sort of 256 keys held 8 per lane (element lane*8 + r).
+__device__ inline void bitonic_sort_256(unsigned long long (&v)[8]) { bitonic<8>(v); }
+
+// Sequential f32 sum of B[0..count) (global workspace, 16-byte aligned) by
+// lane 0, in order, staged through the warp's shared area S (STAGE_TERMS
+// floats, 16-byte aligned): the warp copies STAGE_TERMS terms at a time into
+// S (zero-padded to a multiple of 8), lane 0 adds them eight per step with its
+// shared loads one step ahead, and with `prefix` the running sums go back to
+// B.  Result broadcast to every lane.  The same additions in the same order
+// as a plain loop, without a global-memory round trip per step.
+constexpr int STAGE_TERMS = 1024;
+
+__device__ __forceinline__ float4 lds4(uint32_t a);
+__device__ __forceinline__ void sts4(uint32_t a, const float4& v);
+
+__device__ float chain_staged(float* B, int count, bool prefix, float* S) {
+  const int lane = (int)lane_id();
   float c = 0.0f;
-  if (lane_id() == 0) {
-    float4* B4 = reinterpret_cast<float4*>(B);
-    const int n4 = count >> 2;
-    if (prefix) {
-      for (int q = 0; q < n4; ++q) {
-        float4 v = B4[q];
-        c = __fadd_rn(c, v.x);
-        v.x = c;
-        c = __fadd_rn(c, v.y);
-        v.y = c;
-        c = __fadd_rn(c, v.z);
-        v.z = c;
-        c = __fadd_rn(c, v.w);
-        v.w = c;
-        B4[q] = v;
+  for (int base = 0; base < count; base += STAGE_TERMS) {
+    const int m = min(STAGE_TERMS, count - base);
+    const int m8 = (m + 7) & ~7;
+    const float4* B4 = reinterpret_cast<const float4*>(B + base);
+    float4* S4 = reinterpret_cast<float4*>(S);
+    for (int q = lane; q < (m >> 2); q += 32) S4[q] = B4[q];
+    for (int j = (m & ~3) + lane; j < m8; j += 32) S[j] = j < m ? B[base + j] : 0.0f;
+    __syncwarp();
+    if (lane == 0) {
+      const uint32_t s0 = smem_u32(S);
+      const int n8 = m8 >> 3;
+      float4 na = lds4(s0), nb = lds4(s0 + 16u);
+      for (int q = 0; q < n8; ++q) {
+        float4 va = na, vb = nb;
+        const uint32_t a = s0 + 32u * (uint32_t)q;
+        if (q + 1 < n8) {
+          na = lds4(a + 32u);
+          nb = lds4(a + 48u);
+        }
+        c = __fadd_rn(c, va.x);
+        va.x = c;
+        c = __fadd_rn(c, va.y);
+        va.y = c;
+        c = __fadd_rn(c, va.z);
+        va.z = c;
+        c = __fadd_rn(c, va.w);
+        va.w = c;
+        c = __fadd_rn(c, vb.x);
+        vb.x = c;
+        c = __fadd_rn(c, vb.y);
+        vb.y = c;
+        c = __fadd_rn(c, vb.z);
+        vb.z = c;
+        c = __fadd_rn(c, vb.w);
+        vb.w = c;
+        if (prefix) {
+          sts4(a, va);
+          sts4(a + 16u, vb);
+        }
       }
-      for (int j = n4 << 2; j < count; ++j) {
-        c = __fadd_rn(c, B[j]);
-        B[j] = c;
-      }
-    } else {
-      for (int q = 0; q < n4; ++q) {
-        const float4 v = B4[q];
-        c = __fadd_rn(c, v.x);
-        c = __fadd_rn(c, v.y);
-        c = __fadd_rn(c, v.z);
-        c = __fadd_rn(c, v.w);
-      }
-      for (int j = n4 << 2; j < count; ++j) c = __fadd_rn(c, B[j]);
     }
+    __syncwarp();
+    if (prefix) {
+      float4* W4 = reinterpret_cast<float4*>(B + base);
+      for (int q = lane; q < (m >> 2); q += 32) W4[q] = S4[q];
+      for (int j = (m & ~3) + lane; j < m; j += 32) B[base + j] = S[j];
+    }
+    __syncwarp();
+    c = __shfl_sync(FULL, c, 0);
   }
-  __syncwarp();
-  return __shfl_sync(FULL, c, 0);
+  return c;
 }
 
 __device__ __forceinline__ unsigned long long nucleus_key(float p, uint16_t idx) {
@@ -549,19 +590,201 @@ __device__ __forceinline__ unsigned long long pack_top_p(int status, int ns, flo
          __float_as_uint(m2);
 }
 
-// Top-p over a survivor list in vocabulary order (sampling.rs:665-698): the
-// full-vocabulary softmax denominator, the max - 16 cutoff and the nucleus
-// walked in (p desc, index asc) order, 256 at a time.  On return the list
-// holds the nucleus (vocabulary order, B = exp(x - m2)).  Returns status,
-// nucleus length and m2 packed by pack_top_p.
+template <int R, typename T>
+__device__ __forceinline__ void bitonic(T (&v)[R]);
+
+// Status of top_p_from_candidates when the candidates cannot decide the
+// nucleus (the caller then walks the whole list).
+constexpr int TOPP_UNDECIDED = 0x7F;
+constexpr int TOPP_CANDS = 256;  // candidates one warp sorts in registers (8 per lane)
+
+// The nucleus from the list's largest entries (sampling.rs:665-698).  The
+// reference sorts every entry within 16 of the maximum by (p desc, index
+// asc) and keeps the positions before the first position > 0 whose
+// preceding cumulative reaches top_p.  Here:
+//   * a 64-bucket histogram of x over [m1 - 16, m1] (count and, for sizing
+//     only, the mass of exp(x - m1) per bucket; the map is monotone in x)
+//     picks the fewest top buckets whose mass reaches top_p with a margin;
+//   * their entries (at most TOPP_CANDS) are sorted by (p desc, index asc)
+//     with the reference's p = exp(x - m1) * inv_total, and one lane walks
+//     the sequential f32 cumulative in that order;
+//   * the walk decides the nucleus exactly when it closes inside the
+//     candidates and its last member's p is strictly above the largest p of
+//     any entry outside them (which is then ordered after it), or when the
+//     candidates are every entry within 16 of the maximum.
+// Otherwise one more bucket is tried, then TOPP_UNDECIDED is returned.  On
+// success the list is compacted to the nucleus as apply_top_p leaves it.
+// hist: 128 words; keys: TOPP_CANDS entries.
+__device__ unsigned long long top_p_from_candidates(float* B, float* BX, uint16_t* BI, int ns,
+                                                    float m1, float total, float top_p,
+                                                    unsigned long long* keys, uint32_t* hist) {
+  const int lane = (int)lane_id();
+  const uint32_t lt = lanemask_lt();
+  const float inv_total = __fdiv_rn(1.0f, total);
+  const float cutoff = __fsub_rn(m1, 16.0f);
+  uint32_t* cnt = hist;
+  float* mass = reinterpret_cast<float*>(hist + 64);
+  auto bucket = [&](float x) {
+    const int b = (int)__fmul_rn(__fsub_rn(m1, x), 4.0f);
+    return b > 63 ? 63 : b;
+  };
+  cnt[lane] = 0u;
+  cnt[lane + 32] = 0u;
+  mass[lane] = 0.0f;
+  mass[lane + 32] = 0.0f;
+  __syncwarp();
+  for (int j = lane; j < ns; j += 32) {
+    const float x = BX[j];
+    if (x >= cutoff) {
+      const int b = bucket(x);
+      atomicAdd(&cnt[b], 1u);
+      atomicAdd(&mass[b], B[j]);
+    }
+  }
+  __syncwarp();
+  // Lane l holds buckets 2l and 2l + 1; inclusive prefix counts and masses.
+  const uint32_t c0 = cnt[2 * lane], c1 = cnt[2 * lane + 1];
+  const float w0 = mass[2 * lane], w1 = mass[2 * lane + 1];
+  uint32_t cs = c0 + c1;
+  float ws = w0 + w1;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t a = __shfl_up_sync(FULL, cs, o);
+    const float b = __shfl_up_sync(FULL, ws, o);
+    if (lane >= o) {
+      cs += a;
+      ws += b;
+    }
+  }
+  const uint32_t eligible = __shfl_sync(FULL, cs, 31);
+  // Smallest bucket whose cumulative mass reaches top_p * total, with a
+  // margin for the sizing sums' rounding.
+  const float target = __fmul_rn(__fmul_rn(top_p, total), 1.001f);
+  const bool r0 = ws - w1 >= target, r1 = ws >= target;
+  const unsigned b0 = __ballot_sync(FULL, r0), b1 = __ballot_sync(FULL, r1);
+  int first = 63;
+  if (b0 | b1) {
+    const int l0 = b0 ? __ffs(b0) - 1 : 32, l1 = b1 ? __ffs(b1) - 1 : 32;
+    first = l0 <= l1 ? 2 * l0 : 2 * l1 + 1;
+  }
+  __syncwarp();
+#pragma unroll 1
+  for (int bsel = first; bsel <= first + 1 && bsel <= 63; ++bsel) {
+    // Candidates: entries within 16 of the maximum in buckets <= bsel.
+    const uint32_t ncand = __shfl_sync(FULL, (bsel & 1) ? cs : cs - c1, bsel >> 1);
+    if (ncand > (uint32_t)TOPP_CANDS) break;
+    const bool complete = ncand == eligible;
+    float xout = neg_inf();  // largest x of an entry within 16 outside the candidates
+    int cnt_c = 0;
+    for (int j0 = 0; j0 < ns; j0 += 32) {
+      const int j = j0 + lane;
+      bool in = false;
+      float x = neg_inf();
+      if (j < ns) {
+        x = BX[j];
+        if (x >= cutoff) {
+          if (bucket(x) <= bsel)
+            in = true;
+          else
+            xout = fmaxf(xout, x);
+        }
+      }
+      const unsigned bb = __ballot_sync(FULL, in);
+      if (in) {
+        const float p = __fmul_rn(B[j], inv_total);
+        keys[cnt_c + __popc(bb & lt)] =
+            ((unsigned long long)(~__float_as_uint(p)) << 32) |
+            ((uint32_t)BI[j] << 16) | (uint32_t)j;
+      }
+      cnt_c += __popc(bb);
+    }
+    xout = warp_max(xout);
+    __syncwarp();
+    unsigned long long v[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int e = lane * 8 + r;
+      v[r] = e < cnt_c ? keys[e] : ~0ull;
+    }
+    __syncwarp();
+    bitonic<8>(v);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) keys[lane * 8 + r] = v[r];
+    __syncwarp();
+    // The walk (sampling.rs:690-697) over the sorted candidates.
+    int J = 0;
+    bool closed = false;
+    float plast = 0.0f;
+    if (lane == 0) {
+      float cum = 0.0f;
+      for (int q = 0; q < cnt_c; ++q) {
+        if (q > 0 && cum >= top_p) {
+          closed = true;
+          break;
+        }
+        const float p = __uint_as_float(~(uint32_t)(keys[q] >> 32));
+        cum = __fadd_rn(cum, p);
+        plast = p;
+        J = q + 1;
+      }
+      if (!closed && J == cnt_c && cum >= top_p) closed = true;  // the next entry is masked
+    }
+    J = __shfl_sync(FULL, J, 0);
+    closed = __shfl_sync(FULL, closed ? 1 : 0, 0) != 0;
+    plast = __shfl_sync(FULL, plast, 0);
+    bool ok = complete || closed;
+    if (ok && !complete && xout > neg_inf()) {
+      // Every entry outside the candidates has p <= pout: it sorts after
+      // the last nucleus member when that member's p is larger.
+      const float pout = __fmul_rn(cr_expf(__fsub_rn(xout, m1)), inv_total);
+      ok = plast > pout;
+    }
+    if (!ok) continue;
+    // The nucleus: positions [0, J).  Mark its list positions, take their
+    // maximum x, then compact the list in place with exp(x - m2).
+    uint32_t* marks = hist;  // 128 words: one bit per list position (ns <= 4096)
+    for (int w = lane; w < 128; w += 32) marks[w] = 0u;
+    __syncwarp();
+    float m2 = neg_inf();
+    for (int q = lane; q < J; q += 32) {
+      const uint32_t j = (uint32_t)keys[q] & 0xFFFFu;
+      atomicOr(&marks[j >> 5], 1u << (j & 31));
+      m2 = fmaxf(m2, BX[j]);
+    }
+    m2 = warp_max(m2);
+    __syncwarp();
+    if (!(m2 > neg_inf())) return pack_top_p(Q3S_STATUS_NO_CANDIDATE, 0, 0.0f);
+    int ns2 = 0;
+    for (int j0 = 0; j0 < ns; j0 += 32) {
+      const int j = j0 + lane;
+      const bool p = j < ns && ((marks[j >> 5] >> (j & 31)) & 1u);
+      const int i = p ? BI[j] : 0;
+      const float x = p ? BX[j] : 0.0f;
+      __syncwarp();
+      const unsigned b = __ballot_sync(FULL, p);
+      if (p) {
+        const int d = ns2 + __popc(b & lt);
+        BI[d] = (uint16_t)i;
+        BX[d] = x;
+        B[d] = cr_expf(__fsub_rn(x, m2));
+      }
+      ns2 += __popc(b);
+      __syncwarp();
+    }
+    return pack_top_p(Q3S_STATUS_OK, ns2, m2);
+  }
+  return pack_top_p(TOPP_UNDECIDED, 0, 0.0f);
+}
+
+// Top-p over a survivor list in vocabulary order (sampling.rs:665-698) given
+// its full-vocabulary softmax denominator `total`: the max - 16 cutoff and
+// the nucleus walked in (p desc, index asc) order, 256 at a time.  On return
+// the list holds the nucleus (vocabulary order, B = exp(x - m2)).  Returns
+// status, nucleus length and m2 packed by pack_top_p.
 __device__ unsigned long long apply_top_p(float* B, float* BX, uint16_t* BI, int ns, float m1,
-                                          float top_p, unsigned long long* keys,
+                                          float total, float top_p, unsigned long long* keys,
                                           uint32_t* hist) {
   const unsigned lane = lane_id();
-  // Denominator: sequential f32 sum in vocabulary order.
-  const float total = chain_sum(B, ns, false);
-  if (!is_finite(total) || total <= 0.0f)
-    return pack_top_p(Q3S_STATUS_INVALID_DENOMINATOR, 0, 0.0f);
   const float inv_total = __fdiv_rn(1.0f, total);
   const float cutoff = __fsub_rn(m1, 16.0f);
   int np = 0;
@@ -667,9 +890,11 @@ __device__ unsigned long long apply_top_p(float* B, float* BX, uint16_t* BI, int
 // General path: mask, temperature, top-k, top-p and the draw over the full row
 // held as f32 in A (global workspace).  Kept out of line with scalar and
 // pointer arguments only, so the fast path's state stays in registers.
+// hist: 1024 words (radix histograms, chain staging); hist2: 128 words.
 __device__ __noinline__ unsigned long long general_compute(
     float* A, float* GB, float* GBX, uint16_t* GBI, const uint32_t* bm, uint32_t* hist,
-    unsigned long long* keys, int n, float inv, float pf, int use_pen, int sf, int allow,
+    uint32_t* hist2, unsigned long long* keys, int n, float inv, float pf, int use_pen, int sf,
+    int allow,
     unsigned top_k, int use_top_p, float top_p, float u, unsigned char* masks, float* probs) {
   const unsigned lane = lane_id();
   RowCtx rc;
@@ -738,8 +963,18 @@ __device__ __noinline__ unsigned long long general_compute(
     }
     __syncwarp();
     float m2 = mx;
+    float* S = reinterpret_cast<float*>(hist);  // chain staging (STAGE_TERMS floats)
     if (use_top_p) {
-      const unsigned long long r = apply_top_p(GB, GBX, GBI, ns, mx, top_p, keys, hist);
+      // Denominator: sequential f32 sum in vocabulary order (sampling.rs:666-679).
+      const float total = chain_staged(GB, ns, false, S);
+      unsigned long long r;
+      if (!is_finite(total) || total <= 0.0f) {
+        r = pack_top_p(Q3S_STATUS_INVALID_DENOMINATOR, 0, 0.0f);
+      } else {
+        r = top_p_from_candidates(GB, GBX, GBI, ns, mx, total, top_p, keys, hist2);
+        if ((int)(r >> 56) == TOPP_UNDECIDED)
+          r = apply_top_p(GB, GBX, GBI, ns, mx, total, top_p, keys, hist);
+      }
       const int st = (int)(r >> 56);
       if (st != Q3S_STATUS_OK) {
         out = {st, 0u};
@@ -751,7 +986,7 @@ __device__ __noinline__ unsigned long long general_compute(
     }
     if (ns >= 0) {
       // Final softmax sum and the draw (sampling.rs:700-729).
-      const float sum = chain_sum(GB, ns, true);
+      const float sum = chain_staged(GB, ns, true, S);
       if (!is_finite(sum) || sum <= 0.0f) {
         out = {Q3S_STATUS_INVALID_DENOMINATOR, 0u};
       } else {
@@ -862,6 +1097,30 @@ __device__ __forceinline__ float scan_stage(const FastSpace& f, const RowCtx& r,
     mx = fmaxf(mx, m);
   }
   return warp_max(mx);
+}
+
+// Penalty, suppression and temperature (sampling.rs:592-631) applied in place
+// to an f32 row in its stage, each lane over its own scan chunk, as a rolled
+// loop: the scan that follows is the plain one, and its unrolled body stays
+// small.  The values written are xform's, so they equal what the collection
+// recomputes from the row in global memory.  With EDGE, entries outside
+// [0, n) become -inf (the scan masks them by index as well).
+template <int NJ, bool EDGE>
+__device__ __forceinline__ void xform_stage_f32(const FastSpace& f, const RowCtx& r) {
+  const int lane = (int)lane_id();
+  const int sw = lane & 7;
+  uint4* chunk = reinterpret_cast<uint4*>(f.stage) + lane * NJ;
+#pragma unroll 1
+  for (int j = 0; j < NJ; ++j) {
+    const int v = (j & ~7) | ((j & 7) ^ sw);
+    uint4 w = chunk[v];
+    const int i0 = (lane * NJ + v) * 4 - r.mis;
+    w.x = __float_as_uint(xform<true, EDGE>(__uint_as_float(w.x), i0, r));
+    w.y = __float_as_uint(xform<true, EDGE>(__uint_as_float(w.y), i0 + 1, r));
+    w.z = __float_as_uint(xform<true, EDGE>(__uint_as_float(w.z), i0 + 2, r));
+    w.w = __float_as_uint(xform<true, EDGE>(__uint_as_float(w.w), i0 + 3, r));
+    chunk[v] = w;
+  }
 }
 
 // Bit v set when chunk vector v of this lane has its maximum >= tau.
@@ -1029,31 +1288,36 @@ __device__ __forceinline__ int collect_cands(const RowCtx& r, uint32_t flags, fl
 // ===========================================================================
 
 __device__ __forceinline__ float ex(const uint2& e) { return __uint_as_float(e.x); }
-__device__ __forceinline__ uint32_t kx(const uint2& e) { return total_key(__uint_as_float(e.x)); }
 
 // Ascending bitonic sort of 32*R keys held R per lane (element lane*R + r);
-// R is a power of two.
+// R is a power of two.  The merge sizes and the cross-lane strides (>= R) are
+// loops: only the R register operations of one step are unrolled, plus the
+// log2(R) in-lane steps whose register pairs must be static.  The sorts run
+// on rows that reach the finishers; straight-line code for all 36 steps of a
+// 256-key sort would evict the hot path from the instruction cache.
 template <int R, typename T>
 __device__ __forceinline__ void bitonic(T (&v)[R]) {
-  const unsigned lane = lane_id();
-#pragma unroll
+  const int lane = (int)lane_id();
+#pragma unroll 1
   for (int size = 2; size <= 32 * R; size <<= 1) {
+#pragma unroll 1
+    for (int stride = size >> 1; stride >= R; stride >>= 1) {
+      const int ls = stride / R;
+      const bool lower = (lane & ls) == 0;
 #pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      if (stride >= R) {
-        const int ls = stride / R;
-        const bool lower = (lane & ls) == 0;
+      for (int r = 0; r < R; ++r) {
+        const bool up = ((lane * R + r) & size) == 0;
+        const T o = __shfl_xor_sync(FULL, v[r], ls);
+        v[r] = (lower == up) ? (o < v[r] ? o : v[r]) : (o > v[r] ? o : v[r]);
+      }
+    }
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const bool up = (((int)lane * R + r) & size) == 0;
-          const T o = __shfl_xor_sync(FULL, v[r], ls);
-          v[r] = (lower == up) ? (o < v[r] ? o : v[r]) : (o > v[r] ? o : v[r]);
-        }
-      } else {
+    for (int stride = R >> 1; stride > 0; stride >>= 1) {
+      if (stride < size) {
 #pragma unroll
         for (int r = 0; r < R; ++r) {
           if ((r & stride) == 0) {
-            const bool up = (((int)lane * R + r) & size) == 0;
+            const bool up = ((lane * R + r) & size) == 0;
             const T a = v[r], b = v[r + stride];
             if ((a > b) == up) {
               v[r] = b;
@@ -1066,148 +1330,8 @@ __device__ __forceinline__ void bitonic(T (&v)[R]) {
   }
 }
 
-// Register slot `slot` of v held by lane `owner`, broadcast.
-template <int R, typename T>
-__device__ __forceinline__ T pick(const T (&v)[R], int owner, int slot) {
-  T x = v[0];
-#pragma unroll
-  for (int r = 1; r < R; ++r)
-    if (r == slot) x = v[r];
-  return __shfl_sync(FULL, x, owner);
-}
-
 __device__ __forceinline__ unsigned long long pack_out(int status, uint32_t token) {
   return ((unsigned long long)(unsigned)status << 32) | token;
-}
-
-// Finishes a row from its candidates L[0..c) (x bits, index), k <= c <= 32*R:
-// the statements of sampling.rs:654-729 on the candidate set, which holds
-// every value >= the k-th largest.  Sort keys are 32-bit: (~total_key(x)) for
-// the selection, (index << 16 | list position) for vocabulary order.  Writes
-// the top-k threshold to tsm[0].  Inlined: an out-of-line call here makes
-// the register allocator spill around the hot path of rows without top-p.
-template <int R>
-__device__ __forceinline__ unsigned long long finish_warp(const uint2* L, int c, int k, int n,
-                                                      float Mx, float u, int use_top_p,
-                                                      float top_p, float* Bb,
-                                                      unsigned long long* Kb, float* tsm,
-                                                      unsigned char* masks, float* probs) {
-  constexpr uint32_t NONE = 0xFFFFFFFFu;
-  const int lane = (int)lane_id();
-  // Sort 1: x descending; the k-th largest value is at position k - 1.
-  uint32_t v[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const int e = lane * R + r;
-    v[r] = e < c ? ~kx(L[e]) : NONE;
-  }
-  bitonic<R>(v);
-  const uint32_t tk = pick<R>(v, (k - 1) / R, (k - 1) % R);
-  const float t = from_total_key(~tk);
-  if (lane == 0) tsm[0] = t;
-  // Sort 2: survivors x >= t (sampling.rs:657-662) by vocabulary index.
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const int e = lane * R + r;
-    uint32_t key = NONE;
-    if (e < c) {
-      const uint2 en = L[e];
-      if (ex(en) >= t) key = (en.y << 16) | (uint32_t)e;
-    }
-    v[r] = key;
-  }
-  bitonic<R>(v);
-  int s = 0;
-#pragma unroll
-  for (int r = 0; r < R; ++r) s += v[r] != NONE ? 1 : 0;
-  s = (int)__reduce_add_sync(FULL, (unsigned)s);
-  float xr[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) xr[r] = v[r] != NONE ? ex(L[v[r] & 0xFFFFu]) : neg_inf();
-  float m2 = Mx;
-  int ns = s;
-  if (use_top_p) {
-    // Denominator in vocabulary order (sampling.rs:666-679).
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-      Bb[lane * R + r] = v[r] != NONE ? cr_expf(__fsub_rn(xr[r], Mx)) : 0.0f;
-    __syncwarp();
-    const float total = chain_sum(Bb, s, false);
-    if (!is_finite(total) || total <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
-    const float inv_total = __fdiv_rn(1.0f, total);
-    const float cutoff = __fsub_rn(Mx, 16.0f);
-    // Sort 3: (p desc, index asc) over the entries within 16 of the maximum.
-    unsigned long long w[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      w[r] = ~0ull;
-      if (v[r] != NONE && xr[r] >= cutoff) {
-        const float p = __fmul_rn(Bb[lane * R + r], inv_total);
-        w[r] = ((unsigned long long)(~__float_as_uint(p)) << 32) | v[r];
-      }
-    }
-    bitonic<R>(w);
-#pragma unroll
-    for (int r = 0; r < R; ++r) Kb[lane * R + r] = w[r];
-    __syncwarp();
-    // The nucleus: positions before the first position > 0 whose preceding
-    // cumulative reaches top_p (sampling.rs:690-697).
-    int J = 0;
-    if (lane == 0) {
-      float cum = 0.0f;
-      for (int q = 0; q < 32 * R; ++q) {
-        const unsigned long long key = Kb[q];
-        if (key == ~0ull) break;
-        if (q > 0 && cum >= top_p) break;
-        cum = __fadd_rn(cum, __uint_as_float(~(uint32_t)(key >> 32)));
-        J = q + 1;
-      }
-    }
-    J = __shfl_sync(FULL, J, 0);
-    // Sort 4: the nucleus back into vocabulary order.
-#pragma unroll
-    for (int r = 0; r < R; ++r) v[r] = lane * R + r < J ? (uint32_t)w[r] : NONE;
-    bitonic<R>(v);
-    ns = J;
-    m2 = neg_inf();
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      xr[r] = v[r] != NONE ? ex(L[v[r] & 0xFFFFu]) : neg_inf();
-      m2 = fmaxf(m2, xr[r]);
-    }
-    m2 = warp_max(m2);
-    if (!(m2 > neg_inf())) return pack_out(Q3S_STATUS_NO_CANDIDATE, 0u);
-  }
-  // Final softmax and the vocabulary-order draw (sampling.rs:700-729).
-#pragma unroll
-  for (int r = 0; r < R; ++r)
-    Bb[lane * R + r] = lane * R + r < ns ? cr_expf(__fsub_rn(xr[r], m2)) : 0.0f;
-  __syncwarp();
-  const float sum = chain_sum(Bb, ns, true);
-  if (!is_finite(sum) || sum <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
-  const float thr = __fmul_rn(u, sum);
-  uint32_t first = NONE;
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const int e = lane * R + r;
-    if (e < ns && Bb[e] >= thr) first = min(first, (uint32_t)e);
-  }
-  first = __reduce_min_sync(FULL, first);
-  uint32_t token = (uint32_t)(n - 1);
-  if (first != NONE) token = pick<R>(v, (int)first / R, (int)first % R) >> 16;
-  if (masks || probs) {
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      if (lane * R + r < ns) {
-        const uint32_t i = v[r] >> 16;
-        if (masks) masks[i] |= 4;
-        if (probs)
-          probs[i] = __double2float_rn((double)cr_expf(__fsub_rn(xr[r], m2)) / (double)sum);
-      }
-    }
-  }
-  __syncwarp();
-  return pack_out(Q3S_STATUS_OK, token);
 }
 
 // exp(x) for x <= 0 (finite or -inf): cr_expf without the NaN and overflow
@@ -1257,11 +1381,12 @@ __device__ __forceinline__ void sts4(uint32_t a, const float4& v) {
                : "memory");
 }
 
-// Sequential f32 prefix sums of B[0..count) in place by lane 0 (B in shared
-// memory, 16-byte aligned and zero-padded to a multiple of 8); returns the
-// total to every lane.  Eight terms per step, loads one step ahead of the
-// additions.
-__device__ __forceinline__ float chain_prefix(float* B, int count) {
+// Sequential f32 sum of B[0..count) by lane 0 (B in shared memory, 16-byte
+// aligned and zero-padded to a multiple of 8), with the running sums written
+// back in place when PREFIX is set; returns the total to every lane.  Eight
+// terms per step, loads one step ahead of the additions.
+template <bool PREFIX>
+__device__ __forceinline__ float chain_smem(float* B, int count) {
   float c = 0.0f;
   if (lane_id() == 0) {
     const uint32_t base = smem_u32(B);
@@ -1294,37 +1419,65 @@ __device__ __forceinline__ float chain_prefix(float* B, int count) {
       vb.z = c;
       c = __fadd_rn(c, vb.w);
       vb.w = c;
-      sts4(a, va);
-      sts4(a + 16u, vb);
+      if (PREFIX) {
+        sts4(a, va);
+        sts4(a + 16u, vb);
+      }
     }
   }
   __syncwarp();
   return __shfl_sync(FULL, c, 0);
 }
 
-// Finishes a row without top-p from its candidates L[0..c) in vocabulary
-// order (x after the temperature, index), k <= c <= ROW_CAP: the statements
-// of sampling.rs:654-663 and 700-729 on the candidate set, which holds every
-// element >= the k-th largest x (all others are masked by top-k).
-//   * t, the k-th largest x (ties kept): a 64-bucket histogram (count,
-//     largest and smallest order key per bucket) of the candidates in a
-//     value interval [a, b] (first [lo, Mx]) locates the bucket holding the
-//     k-th largest.  When t is the bucket's largest or smallest value it is
-//     read off directly; a bucket of at most 32 values is ranked exactly; a
-//     fuller one becomes the next interval (its own smallest and largest
-//     value, which land in different buckets, so every level shrinks it).
-//     The bucket map is monotone, so a bucket's members are exactly the
-//     candidates between its smallest and largest value.
-//   * The survivors x >= t are compacted in place, still in vocabulary
-//     order, with exp(x - Mx) in Bb (masked entries are exact zeros of the
-//     reference's sums and are skipped); one lane accumulates the sequential
-//     f32 prefix sums, and the draw is the first survivor whose running sum
-//     reaches u * sum.
-// h: the histogram (HIST_WORDS - 16 words); Bb: ROW_CAP + 8 floats (also the
-// gather space).  Writes t to tsm[0].
-__device__ __forceinline__ unsigned long long finish_topk_hist(
-    uint2* L, int c, int k, int n, float Mx, float lo, float u, float* Bb, uint32_t* h,
-    float* tsm, unsigned char* masks, float* probs) {
+// Final softmax over the survivors L[0..ns) (vocabulary order, every x <= m2,
+// their maximum) and the vocabulary-order draw (sampling.rs:700-729):
+// exp(x - m2) in Bb (zero-padded to a multiple of 8), one lane's sequential
+// f32 prefix sums, and the first survivor whose running sum reaches u * sum
+// (the last index of the row when none does).  Bb: ns + 8 floats.
+__device__ __forceinline__ unsigned long long draw_tail(const uint2* L, int ns, int n, float m2,
+                                                        float u, float* Bb, unsigned char* masks,
+                                                        float* probs) {
+  const int lane = (int)lane_id();
+  for (int j = lane; j < ns; j += 32) Bb[j] = cr_expf_nonpos(__fsub_rn(ex(L[j]), m2));
+  if (lane < ((8 - (ns & 7)) & 7)) Bb[ns + lane] = 0.0f;  // zero-pad to a multiple of 8
+  __syncwarp();
+  const float sum = chain_smem<true>(Bb, ns);
+  if (!is_finite(sum) || sum <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
+  const float thr = __fmul_rn(u, sum);
+  uint32_t token = (uint32_t)(n - 1);
+  for (int j0 = 0; j0 < ns; j0 += 32) {
+    const int j = j0 + lane;
+    const unsigned bb = __ballot_sync(FULL, j < ns && Bb[j] >= thr);
+    if (bb) {
+      token = L[j0 + __ffs(bb) - 1].y;
+      break;
+    }
+  }
+  if (masks || probs) {
+    for (int j = lane; j < ns; j += 32) {
+      const uint2 en = L[j];
+      if (masks) masks[en.y] |= 4;
+      if (probs)
+        probs[en.y] = __double2float_rn((double)cr_expf(__fsub_rn(ex(en), m2)) / (double)sum);
+    }
+  }
+  __syncwarp();
+  return pack_out(Q3S_STATUS_OK, token);
+}
+
+// t, the k-th largest x of the candidates L[0..c) (x after the temperature,
+// index), k <= c <= ROW_CAP, ties kept (sampling.rs:654-663): a 64-bucket
+// histogram (count, largest and smallest order key per bucket) of the
+// candidates in a value interval [a, b] (first [lo, Mx]) locates the bucket
+// holding the k-th largest.  When t is the bucket's largest or smallest value
+// it is read off directly; a bucket of at most 32 values is ranked exactly; a
+// fuller one becomes the next interval (its own smallest and largest value,
+// which land in different buckets, so every level shrinks it).  The bucket
+// map is monotone, so a bucket's members are exactly the candidates between
+// its smallest and largest value.  h: the histogram (HIST_WORDS - 16 words);
+// Bb: 32 floats of gather space.
+__device__ __forceinline__ float kth_largest(const uint2* L, int c, int k, float Mx, float lo,
+                                             float* Bb, uint32_t* h) {
   const int lane = (int)lane_id();
   const uint32_t lt = lanemask_lt();
   float t = Mx;
@@ -1413,9 +1566,14 @@ __device__ __forceinline__ unsigned long long finish_topk_hist(
       __syncwarp();
     }
   }
-  if (lane == 0) tsm[0] = t;
-  // Survivors, compacted in place (d <= j, and every read of an iteration
-  // precedes its writes), then their softmax numerators.
+  return t;
+}
+
+// Keeps the candidates x >= t, compacted in place in vocabulary order (d <= j,
+// and every read of an iteration precedes its writes); returns their number.
+__device__ __forceinline__ int compact_ge(uint2* L, int c, float t) {
+  const int lane = (int)lane_id();
+  const uint32_t lt = lanemask_lt();
   int ns = 0;
   for (int j0 = 0; j0 < c; j0 += 32) {
     const int j = j0 + lane;
@@ -1430,31 +1588,120 @@ __device__ __forceinline__ unsigned long long finish_topk_hist(
     ns += __popc(bb);
   }
   __syncwarp();
+  return ns;
+}
+
+// Finishes a row without top-p from its candidates L[0..c) in vocabulary
+// order, k <= c <= ROW_CAP: the statements of sampling.rs:654-663 and
+// 700-729 on the candidate set, which holds every element >= the k-th
+// largest x (all others are masked by top-k).  The survivors x >= t are
+// compacted in place, still in vocabulary order, with exp(x - Mx) in Bb
+// (masked entries are exact zeros of the reference's sums and are skipped);
+// one lane accumulates the sequential f32 prefix sums, and the draw is the
+// first survivor whose running sum reaches u * sum.  Bb: ROW_CAP + 8 floats.
+// Writes t to tsm[0].
+__device__ __forceinline__ unsigned long long finish_topk_hist(
+    uint2* L, int c, int k, int n, float Mx, float lo, float u, float* Bb, uint32_t* h,
+    float* tsm, unsigned char* masks, float* probs) {
+  const int lane = (int)lane_id();
+  const float t = kth_largest(L, c, k, Mx, lo, Bb, h);
+  if (lane == 0) tsm[0] = t;
+  const int ns = compact_ge(L, c, t);
+  return draw_tail(L, ns, n, Mx, u, Bb, masks, probs);
+}
+
+// Status of finish_topp_hist when the survivors outnumber its sort (the row
+// then takes the general path).
+constexpr int WIDE_GENERAL = 0x7E;
+
+// Finishes a top-p row from its candidates L[0..c) in vocabulary order,
+// k <= c <= ROW_CAP (sampling.rs:654-729): the exact k-th largest t and the
+// survivors x >= t as in finish_topk_hist; the top-p denominator, the
+// sequential f32 sum of exp(x - Mx) over the survivors in vocabulary order
+// (every other entry is masked, an exact zero of the reference's sum); the
+// survivors within 16 of the maximum sorted by (p desc, index asc), p =
+// exp(x - Mx) * inv_total, in one register sort of 64-bit keys; one lane
+// walks the cumulative; the nucleus is compacted in place (vocabulary order)
+// and drawn by draw_tail with its own maximum.  More than 256 survivors:
+// WIDE_GENERAL.  Bb and Kb alias (the terms are read before the keys are
+// stored); h: 8 words for the nucleus marks.
+__device__ __forceinline__ unsigned long long finish_topp_hist(
+    uint2* L, int c, int k, int n, float Mx, float lo, float u, float top_p, float* Bb,
+    unsigned long long* Kb, uint32_t* h, float* tsm, unsigned char* masks, float* probs) {
+  const int lane = (int)lane_id();
+  const uint32_t lt = lanemask_lt();
+  const float t = kth_largest(L, c, k, Mx, lo, Bb, h);
+  if (lane == 0) tsm[0] = t;
+  const int ns = compact_ge(L, c, t);
+  if (ns > 256) return pack_out(WIDE_GENERAL, 0u);
+  // Denominator (sampling.rs:666-679).
   for (int j = lane; j < ns; j += 32) Bb[j] = cr_expf_nonpos(__fsub_rn(ex(L[j]), Mx));
   if (lane < ((8 - (ns & 7)) & 7)) Bb[ns + lane] = 0.0f;  // zero-pad to a multiple of 8
   __syncwarp();
-  const float sum = chain_prefix(Bb, ns);
-  if (!is_finite(sum) || sum <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
-  const float thr = __fmul_rn(u, sum);
-  uint32_t token = (uint32_t)(n - 1);
-  for (int j0 = 0; j0 < ns; j0 += 32) {
-    const int j = j0 + lane;
-    const unsigned bb = __ballot_sync(FULL, j < ns && Bb[j] >= thr);
-    if (bb) {
-      token = L[j0 + __ffs(bb) - 1].y;
-      break;
-    }
-  }
-  if (masks || probs) {
-    for (int j = lane; j < ns; j += 32) {
+  const float total = chain_smem<false>(Bb, ns);
+  if (!is_finite(total) || total <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
+  const float inv_total = __fdiv_rn(1.0f, total);
+  const float cutoff = __fsub_rn(Mx, 16.0f);
+  // (p desc, index asc) over the entries within 16 of the maximum
+  // (sampling.rs:680-689); low bits: index, then list position.
+  unsigned long long v[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const int j = lane * 8 + r;
+    v[r] = ~0ull;
+    if (j < ns) {
       const uint2 en = L[j];
-      if (masks) masks[en.y] |= 4;
-      if (probs)
-        probs[en.y] = __double2float_rn((double)cr_expf(__fsub_rn(ex(en), Mx)) / (double)sum);
+      if (ex(en) >= cutoff) {
+        const float p = __fmul_rn(Bb[j], inv_total);
+        v[r] = ((unsigned long long)(~__float_as_uint(p)) << 32) | (en.y << 16) | (uint32_t)j;
+      }
     }
   }
   __syncwarp();
-  return pack_out(Q3S_STATUS_OK, token);
+  bitonic<8>(v);
+#pragma unroll
+  for (int r = 0; r < 8; ++r) Kb[lane * 8 + r] = v[r];
+  __syncwarp();
+  // The nucleus: positions before the first position > 0 whose preceding
+  // cumulative reaches top_p (sampling.rs:690-697).
+  int J = 0;
+  if (lane == 0) {
+    float cum = 0.0f;
+    for (int q = 0; q < 256; ++q) {
+      const unsigned long long key = Kb[q];
+      if (key == ~0ull) break;
+      if (q > 0 && cum >= top_p) break;
+      cum = __fadd_rn(cum, __uint_as_float(~(uint32_t)(key >> 32)));
+      J = q + 1;
+    }
+  }
+  J = __shfl_sync(FULL, J, 0);
+  if (lane < 8) h[lane] = 0u;
+  __syncwarp();
+  for (int q = lane; q < J; q += 32) {
+    const uint32_t j = (uint32_t)Kb[q] & 0xFFFFu;
+    atomicOr(&h[j >> 5], 1u << (j & 31));
+  }
+  __syncwarp();
+  // Compact the nucleus in place (vocabulary order kept) and take its maximum.
+  int n2 = 0;
+  float m2 = neg_inf();
+  for (int j0 = 0; j0 < ns; j0 += 32) {
+    const int j = j0 + lane;
+    const bool keep = j < ns && ((h[j >> 5] >> (j & 31)) & 1u);
+    uint2 en = make_uint2(0u, 0u);
+    if (keep) {
+      en = L[j];
+      m2 = fmaxf(m2, ex(en));
+    }
+    const unsigned bb = __ballot_sync(FULL, keep);
+    if (keep) L[n2 + __popc(bb & lt)] = en;
+    n2 += __popc(bb);
+  }
+  __syncwarp();
+  m2 = warp_max(m2);
+  if (!(m2 > neg_inf())) return pack_out(Q3S_STATUS_NO_CANDIDATE, 0u);
+  return draw_tail(L, n2, n, m2, u, Bb, masks, probs);
 }
 
 // Debug pass over the stage: bit0 finite x, bit1 x >= t (OR-ed in).
@@ -1485,7 +1732,14 @@ __device__ int fast_front(const FastSpace& f, int k, bool use_top_p, const RowCt
                           Releaser& rel, float& delta, RowOut& out, int& c_out, float& Mx_out,
                           float& lo_out) {
   float vm[NJ];
-  const float mx = scan_stage<DT, NJ, XF, EDGE>(f, rc, vm);
+  float mx;
+  if (XF && DT == Q3S_DTYPE_F32) {
+    // f32 rows are transformed in the stage first; the scan is then plain.
+    xform_stage_f32<NJ, EDGE>(f, rc);
+    mx = scan_stage<DT, NJ, false, EDGE>(f, rc, vm);
+  } else {
+    mx = scan_stage<DT, NJ, XF, EDGE>(f, rc, vm);
+  }
   release<DT>(rel);  // everything below reads the row from global memory
   if (!XF && mx == __int_as_float(0x7f800000)) return FRONT_GENERAL;  // raw +inf
   if (mx == neg_inf() || mx != mx) {
@@ -1519,7 +1773,6 @@ __device__ int fast_front(const FastSpace& f, int k, bool use_top_p, const RowCt
   const int c = collect_cands<DT, NJ, XF, EDGE>(rc, flags, tau,
                                                 reinterpret_cast<uint16_t*>(f.Kb), f.list);
   if (c < k) return FRONT_GENERAL;  // more than ROW_CAP candidates (or none: impossible)
-  if (use_top_p && c > 256) return FRONT_GENERAL;  // the sorting finisher holds 256 keys
   c_out = c;
   Mx_out = Mx;
   lo_out = XF ? tau : __fmul_rn(tau, rc.inv);  // every candidate lies in [lo, Mx]
@@ -1548,6 +1801,257 @@ __device__ RowOut greedy_stage(const FastSpace& f, const StageView& s, int sf, i
   best = warp_max_u64(best);
   if (best == 0ull) return {Q3S_STATUS_NO_CANDIDATE, 0u};
   return {Q3S_STATUS_OK, 0xFFFFFFFFu - (uint32_t)best};
+}
+
+// Top-p without top-k (top_k 0, or at least the vocabulary) on an f32 row
+// held in its stage (sampling.rs:608-729).  The reference takes the softmax
+// denominator over the whole row and walks every entry within 16 of the
+// maximum in (p desc, index asc) order; the nucleus it keeps is, in practice,
+// a small set of the largest entries.  Here:
+//   * the stage is transformed in place to x (penalty, suppression,
+//     temperature) and reduced to its maximum Mx, then transformed again to
+//     e = exp(x - Mx) (entries outside the row and masked entries are exact
+//     zeros); one lane adds the whole stage in vocabulary order, the
+//     reference's sequential f32 denominator;
+//   * a histogram of e by binary exponent (bucket b holds e in
+//     [2^-b, 2^(1-b))) over the entries within 16 of the maximum gives the
+//     deepest bucket B whose cumulative count is at most 256: the entries of
+//     buckets <= B are the candidates, and every other such entry has e
+//     below 2^-B, so p at most pb = 2^-B * inv_total (rounded: the product
+//     is monotone);
+//   * the candidates are sorted by (p desc, index asc) with p = e *
+//     inv_total and walked by one lane; the walk decides the nucleus exactly
+//     when it closed and its last member's p is above pb (every other entry
+//     then sorts after it), or when the candidates are every entry within 16
+//     of the maximum.
+// Two out-of-line halves with scalar and pointer arguments only, so that the
+// fast path's row state stays in registers: nucleus_front (everything that
+// reads the stage; the caller then releases it) and nucleus_finish.  Both
+// return WIDE_GENERAL (the row takes the general path) when the candidates
+// cannot decide the nucleus.
+//
+// nucleus_front's results besides the packed (status, candidate count):
+// hist[1] Mx, hist[2] pb (negative: the candidates are complete), hist[3]
+// the denominator (f32 bits); hist[16 .. 48) holds its histogram.
+__device__ __forceinline__ int ebucket(float e) {
+  const int b = 127 - (int)((__float_as_uint(e) >> 23) & 0xFFu);
+  return b < 0 ? 0 : (b > 31 ? 31 : b);
+}
+
+template <int NJ>
+__device__ __noinline__ unsigned long long nucleus_front(
+    unsigned char* stage, uint2* list, uint32_t* hist, const uint32_t* bm, const uint4* g16,
+    int n, int mis, int Q, float inv, float pf, int use_pen, int sf, int allow, int edge) {
+  const int lane = (int)lane_id();
+  RowCtx rc;
+  rc.n = n;
+  rc.mis = mis;
+  rc.Q = Q;
+  rc.g16 = g16;
+  rc.inv = inv;
+  rc.pf = pf;
+  rc.use_pen = use_pen != 0;
+  rc.sf = sf;
+  rc.allow = allow;
+  rc.bm = bm;
+  const int sw = lane & 7;
+  float4* chunk = reinterpret_cast<float4*>(stage) + lane * NJ;
+  // x in place and its maximum.
+  float mx = neg_inf();
+#pragma unroll 1
+  for (int j = 0; j < NJ; ++j) {
+    const int v = (j & ~7) | ((j & 7) ^ sw);
+    float4 w = chunk[v];
+    const int i0 = (lane * NJ + v) * 4 - mis;
+    if (edge) {
+      w.x = xform<true, true>(w.x, i0, rc);
+      w.y = xform<true, true>(w.y, i0 + 1, rc);
+      w.z = xform<true, true>(w.z, i0 + 2, rc);
+      w.w = xform<true, true>(w.w, i0 + 3, rc);
+    } else {
+      w.x = xform<true, false>(w.x, i0, rc);
+      w.y = xform<true, false>(w.y, i0 + 1, rc);
+      w.z = xform<true, false>(w.z, i0 + 2, rc);
+      w.w = xform<true, false>(w.w, i0 + 3, rc);
+    }
+    mx = fmaxf(mx, fmaxf(fmaxf(w.x, w.y), fmaxf(w.z, w.w)));
+    chunk[v] = w;
+  }
+  mx = warp_max(mx);
+  if (mx == neg_inf())
+    return pack_out(sf >= 0 ? Q3S_STATUS_SUPPRESSION_NO_CANDIDATE : Q3S_STATUS_NO_CANDIDATE, 0u);
+  if (!(mx < __int_as_float(0x7f800000)))  // +inf after the temperature
+    return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
+  const float Mx = mx;
+  const float cutoff = __fsub_rn(Mx, 16.0f);
+  // e in place, with the histogram of the entries within 16 of the maximum.
+  uint32_t* cnt = hist + 16;
+  cnt[lane] = 0u;
+  __syncwarp();
+#pragma unroll 1
+  for (int j = 0; j < NJ; ++j) {
+    const int v = (j & ~7) | ((j & 7) ^ sw);
+    const float4 w = chunk[v];
+    const float x[4] = {w.x, w.y, w.z, w.w};
+    float e[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      e[t] = cr_expf_nonpos(__fsub_rn(x[t], Mx));
+      if (x[t] >= cutoff) atomicAdd(&cnt[ebucket(e[t])], 1u);
+    }
+    chunk[v] = make_float4(e[0], e[1], e[2], e[3]);
+  }
+  __syncwarp();
+  const float total = chain_smem<false>(reinterpret_cast<float*>(stage), 32 * NJ * 4);
+  if (!is_finite(total) || total <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
+  const float inv_total = __fdiv_rn(1.0f, total);
+  // The deepest bucket whose cumulative count still fits 256: the
+  // candidates are as many of the largest entries as the sort holds.
+  uint32_t cs = cnt[lane];
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t a = __shfl_up_sync(FULL, cs, o);
+    if (lane >= o) cs += a;
+  }
+  const uint32_t eligible = __shfl_sync(FULL, cs, 31);
+  const unsigned fit = __ballot_sync(FULL, cs <= 256u);  // a prefix of the buckets
+  if (!(fit & 1u)) return pack_out(WIDE_GENERAL, 0u);   // the top bucket alone is too full
+  const int B = 31 - __clz(fit);
+  const bool complete = __shfl_sync(FULL, cs, B) == eligible;
+  // Candidates: entries of buckets <= B within 16 of the maximum, in
+  // vocabulary order (each lane's chunk is contiguous, lanes in order), with
+  // x recomputed from the row in global memory (the stage now holds e).
+  // Pass 0 counts per lane, pass 1 writes at the lane's offset.
+  int base = 0, c = 0;
+#pragma unroll 1
+  for (int pass = 0; pass < 2; ++pass) {
+    int o = base;
+#pragma unroll 1
+    for (int j = 0; j < NJ; ++j) {
+      const float4 w = chunk[j];
+      const float e[4] = {w.x, w.y, w.z, w.w};
+      uint32_t bits = 0;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) bits |= (e[t] > 0.0f && ebucket(e[t]) <= B ? 1u : 0u) << t;
+      if (bits) {
+        const int q = lane * NJ + j;
+        const uint4 raw = __ldg(g16 + q);
+        const float r[4] = {__uint_as_float(raw.x), __uint_as_float(raw.y),
+                            __uint_as_float(raw.z), __uint_as_float(raw.w)};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          if ((bits >> t) & 1u) {
+            const int i = q * 4 + t - mis;
+            const float x = xform<true, true>(r[t], i, rc);
+            if (x >= cutoff) {
+              if (pass == 1 && o < 256) list[o] = make_uint2(__float_as_uint(x), (uint32_t)i);
+              ++o;
+            }
+          }
+        }
+      }
+    }
+    if (pass == 0) {
+      const int mine = o;
+      const int incl = (int)warp_inclusive_scan((uint32_t)mine);
+      base = incl - mine;
+      c = __shfl_sync(FULL, incl, 31);
+      if (c > 256 || c < 1) return pack_out(WIDE_GENERAL, 0u);
+    }
+  }
+  __syncwarp();
+  const float pb = complete ? -1.0f
+                            : __fmul_rn(__uint_as_float((uint32_t)(127 - B) << 23), inv_total);
+  if (lane == 0) {
+    hist[1] = __float_as_uint(Mx);
+    hist[2] = __float_as_uint(pb);
+    hist[3] = __float_as_uint(total);
+  }
+  __syncwarp();
+  return pack_out(Q3S_STATUS_OK, (uint32_t)c);
+}
+
+__device__ __noinline__ unsigned long long nucleus_finish(uint2* list, unsigned long long* Kb,
+                                                          uint32_t* hist, int c, int n,
+                                                          float top_p, float u,
+                                                          unsigned char* masks, float* probs) {
+  const int lane = (int)lane_id();
+  const uint32_t lt = lanemask_lt();
+  const float Mx = __uint_as_float(hist[1]);
+  const float pb = __uint_as_float(hist[2]);
+  const float total = __uint_as_float(hist[3]);
+  if (!is_finite(total) || total <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
+  const float inv_total = __fdiv_rn(1.0f, total);
+  const float cutoff = __fsub_rn(Mx, 16.0f);
+  unsigned long long v[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const int j = lane * 8 + r;
+    v[r] = ~0ull;
+    if (j < c) {
+      const uint2 en = list[j];
+      if (ex(en) >= cutoff) {
+        const float p = __fmul_rn(cr_expf_nonpos(__fsub_rn(ex(en), Mx)), inv_total);
+        v[r] = ((unsigned long long)(~__float_as_uint(p)) << 32) | (en.y << 16) | (uint32_t)j;
+      }
+    }
+  }
+  bitonic<8>(v);
+#pragma unroll
+  for (int r = 0; r < 8; ++r) Kb[lane * 8 + r] = v[r];
+  __syncwarp();
+  // The walk (sampling.rs:690-697) over the sorted candidates.
+  int J = 0;
+  bool closed = false;
+  float plast = 0.0f;
+  if (lane == 0) {
+    float cum = 0.0f;
+    for (int q = 0; q < 256; ++q) {
+      const unsigned long long key = Kb[q];
+      if (key == ~0ull) break;
+      if (q > 0 && cum >= top_p) {
+        closed = true;
+        break;
+      }
+      const float p = __uint_as_float(~(uint32_t)(key >> 32));
+      cum = __fadd_rn(cum, p);
+      plast = p;
+      J = q + 1;
+    }
+    if (!closed && cum >= top_p) closed = true;  // the next entry, if any, is masked
+  }
+  J = __shfl_sync(FULL, J, 0);
+  closed = __shfl_sync(FULL, closed ? 1 : 0, 0) != 0;
+  plast = __shfl_sync(FULL, plast, 0);
+  if (pb >= 0.0f) {  // some entry outside the candidates is within 16 of the maximum
+    if (!closed || !(plast > pb)) return pack_out(WIDE_GENERAL, 0u);
+  }
+  uint32_t* marks = hist + 16;  // 8 words: one bit per candidate position
+  if (lane < 8) marks[lane] = 0u;
+  __syncwarp();
+  for (int q = lane; q < J; q += 32) {
+    const uint32_t j = (uint32_t)Kb[q] & 0xFFFFu;
+    atomicOr(&marks[j >> 5], 1u << (j & 31));
+  }
+  __syncwarp();
+  int n2 = 0;
+  float m2 = neg_inf();
+  for (int j0 = 0; j0 < c; j0 += 32) {
+    const int j = j0 + lane;
+    const bool keep = j < c && ((marks[j >> 5] >> (j & 31)) & 1u);
+    uint2 en = make_uint2(0u, 0u);
+    if (keep) {
+      en = list[j];
+      m2 = fmaxf(m2, ex(en));
+    }
+    const unsigned bb = __ballot_sync(FULL, keep);
+    if (keep) list[n2 + __popc(bb & lt)] = en;
+    n2 += __popc(bb);
+  }
+  __syncwarp();
+  m2 = warp_max(m2);
+  if (!(m2 > neg_inf())) return pack_out(Q3S_STATUS_NO_CANDIDATE, 0u);
+  return draw_tail(list, n2, n, m2, u, reinterpret_cast<float*>(Kb), masks, probs);
 }
 
 // A sampled row: fast path when it applies, else the general path.
@@ -1599,17 +2103,12 @@ __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const Gen
       if (!use_top_p) {
         r = finish_topk_hist(f.list, c, k, s.n, Mx, lo, u, Bb, f.hist + 16, tsm, dbg.masks,
                              dbg.probs);
-      } else if (c <= 32) {
-        r = finish_warp<1>(f.list, c, k, s.n, Mx, u, 1, pl.top_p, Bb, f.Kb, tsm, dbg.masks,
-                           dbg.probs);
-      } else if (c <= 128) {
-        r = finish_warp<4>(f.list, c, k, s.n, Mx, u, 1, pl.top_p, Bb, f.Kb, tsm, dbg.masks,
-                           dbg.probs);
       } else {
-        r = finish_warp<8>(f.list, c, k, s.n, Mx, u, 1, pl.top_p, Bb, f.Kb, tsm, dbg.masks,
-                           dbg.probs);
+        r = finish_topp_hist(f.list, c, k, s.n, Mx, lo, u, pl.top_p, Bb, f.Kb, f.hist + 16, tsm,
+                             dbg.masks, dbg.probs);
       }
       out = {(int)(r >> 32), (uint32_t)r};
+      if (out.status == WIDE_GENERAL) goto general;
       if (dbg.masks) {
         __syncwarp();
         if (xf)
@@ -1620,12 +2119,36 @@ __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const Gen
       return out;
     }
   }
+general:
+  if constexpr (DT == Q3S_DTYPE_F32) {
+    // Top-p without top-k: the nucleus from the stage-resident row.
+    if (use_top_p && inv_ok && (pl.k == 0u || pl.k >= (uint32_t)s.n) && s.Q <= 32 * NJ) {
+      const int edge = (s.mis != 0 || (s.n % Elem<DT>::EPV) != 0 || s.Q != 32 * NJ) ? 1 : 0;
+      unsigned long long r = nucleus_front<NJ>(
+          f.stage, f.list, f.hist, f.bm, s.g16, s.n, s.mis, s.Q, rc.inv, rc.pf,
+          rc.use_pen ? 1 : 0, rc.sf, rc.allow, edge);
+      release<DT>(rel);
+      if ((int)(r >> 32) == Q3S_STATUS_OK) {
+        r = nucleus_finish(f.list, f.Kb, f.hist, (int)(uint32_t)r, s.n, pl.top_p, u, dbg.masks,
+                           dbg.probs);
+      }
+      const RowOut out{(int)(r >> 32), (uint32_t)r};
+      if (out.status != WIDE_GENERAL) {
+        if (dbg.masks && out.status == Q3S_STATUS_OK) {
+          __syncwarp();
+          debug_masks<DT, true>(s.p0, rc, neg_inf(), dbg.masks);
+        }
+        return out;
+      }
+    }
+  }
   const unsigned lane = lane_id();
   release<DT>(rel);
   for (int i = lane; i < s.n; i += 32) g.A[i] = load_elem<DT>(s.p0, i);
   __syncwarp();
   const unsigned long long r = general_compute(
-      g.A, g.B, g.BX, g.BI, f.bm, reinterpret_cast<uint32_t*>(f.list), f.Kb, s.n, rc.inv, rc.pf,
+      g.A, g.B, g.BX, g.BI, f.bm, reinterpret_cast<uint32_t*>(f.list), f.hist, f.Kb, s.n, rc.inv,
+      rc.pf,
       rc.use_pen ? 1 : 0, rc.sf, rc.allow, pl.k, use_top_p ? 1 : 0, pl.top_p, u, dbg.masks,
       dbg.probs);
   return {(int)(r >> 32), (uint32_t)r};
@@ -1709,14 +2232,7 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
     // stage copy may still be in flight).
     if (st == Q3S_STATUS_OK && (pflags & PF_USE_PEN)) {
       const long long h0 = a.history_offsets[row], h1 = a.history_offsets[row + 1];
-      const int words = (n + 31) >> 5;
-      for (int w = lane; w < words; w += 32) f.bm[w] = 0u;
-      __syncwarp();
-      for (long long h = h0 + lane; h < h1; h += 32) {
-        const int id = a.history[h];
-        if (id < n) atomicOr(&f.bm[id >> 5], 1u << (id & 31));
-      }
-      __syncwarp();
+      fill_history(a.history + h0, h1 - h0, n, f.bm);
     }
     const bool ready = wait_stage(ctl, slot, gen, a.wait_ns);
     if (!__all_sync(FULL, ready)) {
