@@ -1100,13 +1100,38 @@ __device__ __forceinline__ float scan_stage(const FastSpace& f, const RowCtx& r,
 }
 
 // Penalty, suppression and temperature (sampling.rs:592-631) applied in place
-// to an f32 row in its stage, each lane over its own scan chunk, as a rolled
-// loop: the scan that follows is the plain one, and its unrolled body stays
-// small.  The values written are xform's, so they equal what the collection
-// recomputes from the row in global memory.  With EDGE, entries outside
+// to an f32 row in its stage: the penalty on the history ids, then each lane
+// masks and scales its own scan chunk in a rolled loop, so the scan that
+// follows is the plain one and its unrolled body stays small.  The values
+// written are xform's, so they equal what the collection recomputes from the
+// row in global memory.  With EDGE, entries outside
 // [0, n) become -inf (the scan masks them by index as well).
+// The repetition penalty (sampling.rs:732-773) on the raw f32 row in its
+// stage, element i at row[i]: one update per set bit of the history bitmap,
+// so each distinct id < n is penalised once; the lanes take the bitmap words
+// in turn.
+__device__ __forceinline__ void penalize_stage(float* row, int n, const uint32_t* bm, float pf) {
+  const int lane = (int)lane_id();
+  for (int w = lane; w < ((n + 31) >> 5); w += 32) {
+    uint32_t bits = bm[w];
+    while (bits) {
+      const int i = (w << 5) + __ffs(bits) - 1;
+      bits &= bits - 1;
+      const float v = row[i];
+      row[i] = v < 0.0f ? __fmul_rn(v, pf) : __fdiv_rn(v, pf);
+    }
+  }
+  __syncwarp();
+}
+
 template <int NJ, bool EDGE>
-__device__ __forceinline__ void xform_stage_f32(const FastSpace& f, const RowCtx& r) {
+__device__ __forceinline__ void xform_stage_f32(const FastSpace& f, const RowCtx& rp) {
+  // The penalty on the history ids first, then mask and temperature.
+  RowCtx r = rp;
+  if (r.use_pen) {
+    penalize_stage(reinterpret_cast<float*>(f.stage) + r.mis, r.n, r.bm, r.pf);
+    r.use_pen = false;
+  }
   const int lane = (int)lane_id();
   const int sw = lane & 7;
   uint4* chunk = reinterpret_cast<uint4*>(f.stage) + lane * NJ;
@@ -1804,26 +1829,30 @@ __device__ RowOut greedy_stage(const FastSpace& f, const StageView& s, int sf, i
 }
 
 // Top-p without top-k (top_k 0, or at least the vocabulary) on an f32 row
-// held in its stage (sampling.rs:608-729).  The reference takes the softmax
+// held in its stage (sampling.rs:592-729).  The reference takes the softmax
 // denominator over the whole row and walks every entry within 16 of the
 // maximum in (p desc, index asc) order; the nucleus it keeps is, in practice,
-// a small set of the largest entries.  Here:
-//   * the stage is transformed in place to x (penalty, suppression,
-//     temperature) and reduced to its maximum Mx, then transformed again to
-//     e = exp(x - Mx) (entries outside the row and masked entries are exact
-//     zeros); one lane adds the whole stage in vocabulary order, the
+// a small set of the largest entries.  Here, all in the stage:
+//   * the penalty goes to the history ids only (one per set bit of the
+//     history bitmap), then one pass masks, scales by the temperature and
+//     takes the maximum Mx: the stage holds x;
+//   * a histogram of the entries within 16 of the maximum by 0.5-wide
+//     bands of Mx - x gives the deepest band B whose cumulative count is at
+//     most 256; the entries of bands <= B are the candidates (x and index,
+//     in any order), and the largest x of the other entries within 16 of the
+//     maximum, xout, is kept;
+//   * the same pass turns the stage into e = exp(x - Mx) (masked entries
+//     and entries outside the row are exact zeros), and one lane adds the
+//     stage in vocabulary order up to the suppressed range, then the allowed
+//     token inside it: every skipped entry is an exact zero of the
 //     reference's sequential f32 denominator;
-//   * a histogram of e by binary exponent (bucket b holds e in
-//     [2^-b, 2^(1-b))) over the entries within 16 of the maximum gives the
-//     deepest bucket B whose cumulative count is at most 256: the entries of
-//     buckets <= B are the candidates, and every other such entry has e
-//     below 2^-B, so p at most pb = 2^-B * inv_total (rounded: the product
-//     is monotone);
-//   * the candidates are sorted by (p desc, index asc) with p = e *
-//     inv_total and walked by one lane; the walk decides the nucleus exactly
-//     when it closed and its last member's p is above pb (every other entry
-//     then sorts after it), or when the candidates are every entry within 16
-//     of the maximum.
+//   * nucleus_finish sorts the candidates by (p desc, index asc) with
+//     p = e * inv_total and walks them with one lane.  The walk decides the
+//     nucleus exactly when it closed and its last member's p is above
+//     pout = p(xout), the largest p outside the candidates (every other entry
+//     then sorts after it), or when no entry outside them is within 16 of
+//     the maximum.  The nucleus, sorted back into vocabulary order, is drawn
+//     by draw_tail with its own maximum.
 // Two out-of-line halves with scalar and pointer arguments only, so that the
 // fast path's row state stays in registers: nucleus_front (everything that
 // reads the stage; the caller then releases it) and nucleus_finish.  Both
@@ -1831,32 +1860,35 @@ __device__ RowOut greedy_stage(const FastSpace& f, const StageView& s, int sf, i
 // cannot decide the nucleus.
 //
 // nucleus_front's results besides the packed (status, candidate count):
-// hist[1] Mx, hist[2] pb (negative: the candidates are complete), hist[3]
-// the denominator (f32 bits); hist[16 .. 48) holds its histogram.
-__device__ __forceinline__ int ebucket(float e) {
-  const int b = 127 - (int)((__float_as_uint(e) >> 23) & 0xFFu);
-  return b < 0 ? 0 : (b > 31 ? 31 : b);
+// hist[1] Mx, hist[2] xout (-inf: none), hist[3] the denominator (f32
+// bits); hist[16 .. 48) holds its histogram.  The candidates are list[0..c).
+__device__ __forceinline__ int xband(float x, float Mx) {
+  const int b = (int)__fmul_rn(__fsub_rn(Mx, x), 2.0f);
+  return b > 31 ? 31 : b;
 }
 
 template <int NJ>
 __device__ __noinline__ unsigned long long nucleus_front(
-    unsigned char* stage, uint2* list, uint32_t* hist, const uint32_t* bm, const uint4* g16,
-    int n, int mis, int Q, float inv, float pf, int use_pen, int sf, int allow, int edge) {
+    unsigned char* stage, uint2* list, uint32_t* hist, const uint32_t* bm, int n, int mis,
+    float inv, float pf, int use_pen, int sf, int allow, int edge) {
   const int lane = (int)lane_id();
+  const uint32_t lt = lanemask_lt();
+  float* row = reinterpret_cast<float*>(stage) + mis;  // element i at row[i]
+  if (use_pen) penalize_stage(row, n, bm, pf);
   RowCtx rc;
   rc.n = n;
   rc.mis = mis;
-  rc.Q = Q;
-  rc.g16 = g16;
+  rc.Q = 0;
+  rc.g16 = nullptr;
   rc.inv = inv;
   rc.pf = pf;
-  rc.use_pen = use_pen != 0;
+  rc.use_pen = false;
   rc.sf = sf;
   rc.allow = allow;
   rc.bm = bm;
   const int sw = lane & 7;
   float4* chunk = reinterpret_cast<float4*>(stage) + lane * NJ;
-  // x in place and its maximum.
+  // Mask and temperature in place (sampling.rs:608-631), and the maximum.
   float mx = neg_inf();
 #pragma unroll 1
   for (int j = 0; j < NJ; ++j) {
@@ -1884,7 +1916,7 @@ __device__ __noinline__ unsigned long long nucleus_front(
     return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
   const float Mx = mx;
   const float cutoff = __fsub_rn(Mx, 16.0f);
-  // e in place, with the histogram of the entries within 16 of the maximum.
+  // Histogram of the entries within 16 of the maximum by band.
   uint32_t* cnt = hist + 16;
   cnt[lane] = 0u;
   __syncwarp();
@@ -1892,79 +1924,58 @@ __device__ __noinline__ unsigned long long nucleus_front(
   for (int j = 0; j < NJ; ++j) {
     const int v = (j & ~7) | ((j & 7) ^ sw);
     const float4 w = chunk[v];
-    const float x[4] = {w.x, w.y, w.z, w.w};
-    float e[4];
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      e[t] = cr_expf_nonpos(__fsub_rn(x[t], Mx));
-      if (x[t] >= cutoff) atomicAdd(&cnt[ebucket(e[t])], 1u);
-    }
-    chunk[v] = make_float4(e[0], e[1], e[2], e[3]);
+    if (w.x >= cutoff) atomicAdd(&cnt[xband(w.x, Mx)], 1u);
+    if (w.y >= cutoff) atomicAdd(&cnt[xband(w.y, Mx)], 1u);
+    if (w.z >= cutoff) atomicAdd(&cnt[xband(w.z, Mx)], 1u);
+    if (w.w >= cutoff) atomicAdd(&cnt[xband(w.w, Mx)], 1u);
   }
   __syncwarp();
-  const float total = chain_smem<false>(reinterpret_cast<float*>(stage), 32 * NJ * 4);
-  if (!is_finite(total) || total <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
-  const float inv_total = __fdiv_rn(1.0f, total);
-  // The deepest bucket whose cumulative count still fits 256: the
-  // candidates are as many of the largest entries as the sort holds.
+  // The deepest band whose cumulative count still fits 256.
   uint32_t cs = cnt[lane];
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const uint32_t a = __shfl_up_sync(FULL, cs, o);
     if (lane >= o) cs += a;
   }
-  const uint32_t eligible = __shfl_sync(FULL, cs, 31);
-  const unsigned fit = __ballot_sync(FULL, cs <= 256u);  // a prefix of the buckets
-  if (!(fit & 1u)) return pack_out(WIDE_GENERAL, 0u);   // the top bucket alone is too full
+  const unsigned fit = __ballot_sync(FULL, cs <= 256u);  // a prefix of the bands
+  if (!(fit & 1u)) return pack_out(WIDE_GENERAL, 0u);   // the top band alone is too full
   const int B = 31 - __clz(fit);
-  const bool complete = __shfl_sync(FULL, cs, B) == eligible;
-  // Candidates: entries of buckets <= B within 16 of the maximum, in
-  // vocabulary order (each lane's chunk is contiguous, lanes in order), with
-  // x recomputed from the row in global memory (the stage now holds e).
-  // Pass 0 counts per lane, pass 1 writes at the lane's offset.
-  int base = 0, c = 0;
+  // Candidates (bands <= B) and xout; e = exp(x - Mx) in place.
+  float xout = neg_inf();
+  int c = 0;
 #pragma unroll 1
-  for (int pass = 0; pass < 2; ++pass) {
-    int o = base;
-#pragma unroll 1
-    for (int j = 0; j < NJ; ++j) {
-      const float4 w = chunk[j];
-      const float e[4] = {w.x, w.y, w.z, w.w};
-      uint32_t bits = 0;
+  for (int j = 0; j < NJ; ++j) {
+    const int v = (j & ~7) | ((j & 7) ^ sw);
+    const float4 w = chunk[v];
+    const float x[4] = {w.x, w.y, w.z, w.w};
+    const int i0 = (lane * NJ + v) * 4 - mis;
+    float e[4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) bits |= (e[t] > 0.0f && ebucket(e[t]) <= B ? 1u : 0u) << t;
-      if (bits) {
-        const int q = lane * NJ + j;
-        const uint4 raw = __ldg(g16 + q);
-        const float r[4] = {__uint_as_float(raw.x), __uint_as_float(raw.y),
-                            __uint_as_float(raw.z), __uint_as_float(raw.w)};
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          if ((bits >> t) & 1u) {
-            const int i = q * 4 + t - mis;
-            const float x = xform<true, true>(r[t], i, rc);
-            if (x >= cutoff) {
-              if (pass == 1 && o < 256) list[o] = make_uint2(__float_as_uint(x), (uint32_t)i);
-              ++o;
-            }
-          }
-        }
-      }
+    for (int t = 0; t < 4; ++t) {
+      const bool elig = x[t] >= cutoff;
+      const bool cand = elig && xband(x[t], Mx) <= B;
+      if (elig && !cand) xout = fmaxf(xout, x[t]);
+      const unsigned bb = __ballot_sync(FULL, cand);
+      if (cand) list[c + __popc(bb & lt)] = make_uint2(__float_as_uint(x[t]), (uint32_t)(i0 + t));
+      c += __popc(bb);
+      e[t] = cr_expf_nonpos(__fsub_rn(x[t], Mx));
     }
-    if (pass == 0) {
-      const int mine = o;
-      const int incl = (int)warp_inclusive_scan((uint32_t)mine);
-      base = incl - mine;
-      c = __shfl_sync(FULL, incl, 31);
-      if (c > 256 || c < 1) return pack_out(WIDE_GENERAL, 0u);
-    }
+    chunk[v] = make_float4(e[0], e[1], e[2], e[3]);
   }
+  xout = warp_max(xout);
   __syncwarp();
-  const float pb = complete ? -1.0f
-                            : __fmul_rn(__uint_as_float((uint32_t)(127 - B) << 23), inv_total);
+  // Denominator (sampling.rs:666-679): vocabulary order up to the suppressed
+  // range, then the allowed token inside it; everything else is zero.
+  // The chain covers stage positions [0, span): entries below `lim` and the
+  // zeros around them (span is padded to a multiple of 8, so an allowed
+  // token inside the padding is already added in its place).
+  const int lim = (sf >= 0 && sf < n) ? sf : n;
+  const int span = (mis + lim + 7) & ~7;
+  float total = chain_smem<false>(reinterpret_cast<float*>(stage), span);
+  if (lim < n && allow >= span - mis && allow < n) total = __fadd_rn(total, row[allow]);
   if (lane == 0) {
     hist[1] = __float_as_uint(Mx);
-    hist[2] = __float_as_uint(pb);
+    hist[2] = __float_as_uint(xout);
     hist[3] = __float_as_uint(total);
   }
   __syncwarp();
@@ -1976,13 +1987,13 @@ __device__ __noinline__ unsigned long long nucleus_finish(uint2* list, unsigned 
                                                           float top_p, float u,
                                                           unsigned char* masks, float* probs) {
   const int lane = (int)lane_id();
-  const uint32_t lt = lanemask_lt();
   const float Mx = __uint_as_float(hist[1]);
-  const float pb = __uint_as_float(hist[2]);
+  const float xout = __uint_as_float(hist[2]);
   const float total = __uint_as_float(hist[3]);
   if (!is_finite(total) || total <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
   const float inv_total = __fdiv_rn(1.0f, total);
-  const float cutoff = __fsub_rn(Mx, 16.0f);
+  // (p desc, index asc) over the candidates (sampling.rs:680-689); low bits:
+  // index, then list position.
   unsigned long long v[8];
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
@@ -1990,10 +2001,8 @@ __device__ __noinline__ unsigned long long nucleus_finish(uint2* list, unsigned 
     v[r] = ~0ull;
     if (j < c) {
       const uint2 en = list[j];
-      if (ex(en) >= cutoff) {
-        const float p = __fmul_rn(cr_expf_nonpos(__fsub_rn(ex(en), Mx)), inv_total);
-        v[r] = ((unsigned long long)(~__float_as_uint(p)) << 32) | (en.y << 16) | (uint32_t)j;
-      }
+      const float p = __fmul_rn(cr_expf_nonpos(__fsub_rn(ex(en), Mx)), inv_total);
+      v[r] = ((unsigned long long)(~__float_as_uint(p)) << 32) | (en.y << 16) | (uint32_t)j;
     }
   }
   bitonic<8>(v);
@@ -2023,35 +2032,30 @@ __device__ __noinline__ unsigned long long nucleus_finish(uint2* list, unsigned 
   J = __shfl_sync(FULL, J, 0);
   closed = __shfl_sync(FULL, closed ? 1 : 0, 0) != 0;
   plast = __shfl_sync(FULL, plast, 0);
-  if (pb >= 0.0f) {  // some entry outside the candidates is within 16 of the maximum
-    if (!closed || !(plast > pb)) return pack_out(WIDE_GENERAL, 0u);
+  if (xout > neg_inf()) {  // an entry outside the candidates is within 16 of the maximum
+    const float pout = __fmul_rn(cr_expf_nonpos(__fsub_rn(xout, Mx)), inv_total);
+    if (!closed || !(plast > pout)) return pack_out(WIDE_GENERAL, 0u);
   }
-  uint32_t* marks = hist + 16;  // 8 words: one bit per candidate position
-  if (lane < 8) marks[lane] = 0u;
-  __syncwarp();
-  for (int q = lane; q < J; q += 32) {
-    const uint32_t j = (uint32_t)Kb[q] & 0xFFFFu;
-    atomicOr(&marks[j >> 5], 1u << (j & 31));
-  }
-  __syncwarp();
-  int n2 = 0;
+  // The nucleus, positions [0, J), back into vocabulary order: its keys'
+  // low 32 bits are (index << 16 | list position).
+  uint32_t w[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) w[r] = lane * 8 + r < J ? (uint32_t)v[r] : 0xFFFFFFFFu;
+  bitonic<8>(w);
+  uint2* nuc = list + 256;  // the nucleus, in vocabulary order
   float m2 = neg_inf();
-  for (int j0 = 0; j0 < c; j0 += 32) {
-    const int j = j0 + lane;
-    const bool keep = j < c && ((marks[j >> 5] >> (j & 31)) & 1u);
-    uint2 en = make_uint2(0u, 0u);
-    if (keep) {
-      en = list[j];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    if (lane * 8 + r < J) {
+      const uint2 en = list[w[r] & 0xFFFFu];
+      nuc[lane * 8 + r] = en;
       m2 = fmaxf(m2, ex(en));
     }
-    const unsigned bb = __ballot_sync(FULL, keep);
-    if (keep) list[n2 + __popc(bb & lt)] = en;
-    n2 += __popc(bb);
   }
   __syncwarp();
   m2 = warp_max(m2);
   if (!(m2 > neg_inf())) return pack_out(Q3S_STATUS_NO_CANDIDATE, 0u);
-  return draw_tail(list, n2, n, m2, u, reinterpret_cast<float*>(Kb), masks, probs);
+  return draw_tail(nuc, J, n, m2, u, reinterpret_cast<float*>(Kb), masks, probs);
 }
 
 // A sampled row: fast path when it applies, else the general path.
@@ -2124,9 +2128,9 @@ general:
     // Top-p without top-k: the nucleus from the stage-resident row.
     if (use_top_p && inv_ok && (pl.k == 0u || pl.k >= (uint32_t)s.n) && s.Q <= 32 * NJ) {
       const int edge = (s.mis != 0 || (s.n % Elem<DT>::EPV) != 0 || s.Q != 32 * NJ) ? 1 : 0;
-      unsigned long long r = nucleus_front<NJ>(
-          f.stage, f.list, f.hist, f.bm, s.g16, s.n, s.mis, s.Q, rc.inv, rc.pf,
-          rc.use_pen ? 1 : 0, rc.sf, rc.allow, edge);
+      unsigned long long r =
+          nucleus_front<NJ>(f.stage, f.list, f.hist, f.bm, s.n, s.mis, rc.inv, rc.pf,
+                            rc.use_pen ? 1 : 0, rc.sf, rc.allow, edge);
       release<DT>(rel);
       if ((int)(r >> 32) == Q3S_STATUS_OK) {
         r = nucleus_finish(f.list, f.Kb, f.hist, (int)(uint32_t)r, s.n, pl.top_p, u, dbg.masks,
