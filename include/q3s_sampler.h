@@ -175,6 +175,31 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* batch, void* stream);
  * give-up path; production code never calls it. */
 int q3s_context_set_test_hooks(q3s_context* ctx, uint64_t stage_wait_ns, int32_t hold_refill);
 
+/* Diagnostics, no counterpart in the reference: which path of the sampling
+ * kernel each row took.  The reference runs one algorithm on the host; the
+ * kernel decides most rows from a short candidate list and sends the rest to
+ * slower, equally exact paths, and these counts show how often.           */
+#define Q3S_PATH_INVALID 0          /* status set before sampling (validation, vocabulary) */
+#define Q3S_PATH_GREEDY 1           /* do_sample = 0 */
+#define Q3S_PATH_TOPK 2             /* candidate list, top-k finisher */
+#define Q3S_PATH_TOPK_TOPP 3        /* candidate list, top-k then top-p finisher */
+#define Q3S_PATH_FRONT_DONE 4       /* decided by the scan (no candidate, +inf after temperature) */
+#define Q3S_PATH_NUCLEUS 5          /* top-p without top-k from the staged row */
+#define Q3S_PATH_GENERAL_RULES 6    /* general: top_k 0, > 256 or >= vocab; 1/T 0 or inf; bf16 */
+#define Q3S_PATH_GENERAL_INF 7      /* general: +inf raw logit */
+#define Q3S_PATH_GENERAL_TAU 8      /* general: no threshold on the vector maxima */
+#define Q3S_PATH_GENERAL_OVERFLOW 9 /* general: more candidates than the list holds */
+#define Q3S_PATH_GENERAL_WIDE 10    /* general: more than 256 top-k survivors under top-p */
+#define Q3S_PATH_GENERAL_NUCLEUS 11 /* general: the nucleus outgrew its candidates */
+#define Q3S_PATH_COUNT 12
+
+/* stats: NULL (off) or a device array of 2 * Q3S_PATH_COUNT u64.  While set,
+ * every batched launch of `ctx` adds to stats[p] the rows that took path p
+ * and to stats[Q3S_PATH_COUNT + p] the SM clock cycles their warps spent on
+ * them (from taking the row to storing its result).  Nothing is cleared.
+ * Such launches run the kernel's debug build (same results, slower). */
+int q3s_context_set_path_stats(q3s_context* ctx, uint64_t* stats);
+
 /* Bytes of the file-scope device workspace of q3s_sample_batch_static, held on
  * every device that loads the library until the process exits. */
 #define Q3S_STATIC_SCRATCH_BYTES (32u * 1024u * 1024u)

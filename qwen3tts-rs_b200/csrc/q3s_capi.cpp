@@ -79,6 +79,8 @@ struct q3s_context {
   // Testing hooks (q3s_context_set_test_hooks).
   uint64_t test_wait_ns = 0;
   int test_hold_refill = 0;
+  // Diagnostics (q3s_context_set_path_stats).
+  unsigned long long* path_stats = nullptr;
 };
 
 struct q3s_sampler {
@@ -219,6 +221,7 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* b, void* stream) {
   a.probs_stride = b->probs_stride;
   if (ctx->test_wait_ns) a.wait_ns = ctx->test_wait_ns;
   a.hold_refill = ctx->test_hold_refill;
+  a.path_stats = ctx->path_stats;
   int cap = b->vocab < Q3S_MAX_VOCAB ? b->vocab : Q3S_MAX_VOCAB;
   a.vcap = ((cap > 0 ? cap : 1) + 31) / 32 * 32;
   int warps = q3s::sample_max_warps(a.vcap, b->dtype, ctx->smem_optin);
@@ -264,6 +267,12 @@ int q3s_context_set_test_hooks(q3s_context* ctx, uint64_t stage_wait_ns, int32_t
   if (!ctx) return fail(Q3S_E_INVALID_ARGUMENT, "q3s_context_set_test_hooks: NULL context");
   ctx->test_wait_ns = stage_wait_ns;
   ctx->test_hold_refill = hold_refill ? 1 : 0;
+  return Q3S_OK;
+}
+
+int q3s_context_set_path_stats(q3s_context* ctx, uint64_t* stats) {
+  if (!ctx) return fail(Q3S_E_INVALID_ARGUMENT, "q3s_context_set_path_stats: NULL context");
+  ctx->path_stats = reinterpret_cast<unsigned long long*>(stats);
   return Q3S_OK;
 }
 

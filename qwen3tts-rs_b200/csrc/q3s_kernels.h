@@ -38,6 +38,9 @@ struct KernelArgs {
   // every row after a stage's first one waits for a generation nothing issues.
   unsigned long long wait_ns = 1000000000ull;
   int hold_refill = 0;
+  // Diagnostics (q3s_context_set_path_stats): per Q3S_PATH_* row counts and
+  // warp cycles, accumulated by the debug instantiation; NULL in production.
+  unsigned long long* path_stats = nullptr;
 };
 
 size_t sample_smem_per_warp(int vcap, int dtype);

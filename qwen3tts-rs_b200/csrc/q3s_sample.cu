@@ -424,6 +424,7 @@ __device__ __noinline__ void fill_history(const unsigned short* h, long long cnt
 // Per-row transform inputs.
 struct RowCtx {
   int n, mis, Q;
+  int nj;  // vectors per lane chunk of the fast-path scan (runtime-chunk kernels)
   const uint4* g16;  // the row's 16-byte vectors in global memory (stage layout)
   float inv;      // 1 / (temperature as f32)
   float pf;       // repetition penalty as f32
@@ -901,6 +902,7 @@ __device__ __noinline__ unsigned long long general_compute(
   rc.n = n;
   rc.mis = 0;
   rc.Q = 0;
+  rc.nj = 0;
   rc.g16 = nullptr;
   rc.inv = inv;
   rc.pf = pf;
@@ -1075,26 +1077,39 @@ __device__ bool wait_stage(RingCtl* ctl, int slot, uint32_t gen, uint64_t limit_
 // multiple of 8, so the XOR permutes the chunk), and every address is one of
 // 8 per-lane bases plus an immediate offset.  vm[j] is the maximum of that
 // vector.  Vectors past the row hold stale bytes; EDGE rows mask them by
-// index.
-template <int DT, int NJ, bool XF, bool EDGE>
+// index.  RT (runtime chunk): a row that exactly fills 32 chunks of r.nj
+// vectors (r.nj <= NJ, a multiple of 8) scans those without EDGE; its
+// vectors j >= r.nj have maximum -inf.
+template <int DT, int NJ, bool XF, bool EDGE, bool RT>
 __device__ __forceinline__ float scan_stage(const FastSpace& f, const RowCtx& r, float (&vm)[NJ]) {
   constexpr int EPV = Elem<DT>::EPV;
   const int lane = (int)lane_id();
   const int sw = lane & 7;
-  const uint4* chunk = reinterpret_cast<const uint4*>(f.stage) + lane * NJ;
+  const int nj = (RT && !EDGE) ? r.nj : NJ;
+  const uint4* chunk = reinterpret_cast<const uint4*>(f.stage) + lane * nj;
   float mx = neg_inf();
+  // Groups of 8 vectors; a runtime chunk ends at a group boundary (one
+  // uniform test per group after the first).
 #pragma unroll
-  for (int j = 0; j < NJ; ++j) {
-    const int v = (j & ~7) | ((j & 7) ^ sw);
-    const uint4 w = chunk[v];
-    float e[EPV];
-    unpack_vec<DT>(w, e);
-    float m = neg_inf();
+  for (int g = 0; g < NJ / 8; ++g) {
+    if (RT && !EDGE && g > 0 && 8 * g >= nj) {
 #pragma unroll
-    for (int c = 0; c < EPV; ++c)
-      m = fmaxf(m, xform<XF, EDGE>(e[c], (lane * NJ + v) * EPV + c - r.mis, r));
-    vm[j] = m;
-    mx = fmaxf(mx, m);
+      for (int j = 8 * g; j < NJ; ++j) vm[j] = neg_inf();
+      break;
+    }
+#pragma unroll
+    for (int j = 8 * g; j < 8 * g + 8; ++j) {
+      const int v = (j & ~7) | ((j & 7) ^ sw);
+      const uint4 w = chunk[v];
+      float e[EPV];
+      unpack_vec<DT>(w, e);
+      float m = neg_inf();
+#pragma unroll
+      for (int c = 0; c < EPV; ++c)
+        m = fmaxf(m, xform<XF, EDGE>(e[c], (lane * nj + v) * EPV + c - r.mis, r));
+      vm[j] = m;
+      mx = fmaxf(mx, m);
+    }
   }
   return warp_max(mx);
 }
@@ -1124,7 +1139,7 @@ __device__ __forceinline__ void penalize_stage(float* row, int n, const uint32_t
   __syncwarp();
 }
 
-template <int NJ, bool EDGE>
+template <int NJ, bool EDGE, bool RT>
 __device__ __forceinline__ void xform_stage_f32(const FastSpace& f, const RowCtx& rp) {
   // The penalty on the history ids first, then mask and temperature.
   RowCtx r = rp;
@@ -1134,12 +1149,13 @@ __device__ __forceinline__ void xform_stage_f32(const FastSpace& f, const RowCtx
   }
   const int lane = (int)lane_id();
   const int sw = lane & 7;
-  uint4* chunk = reinterpret_cast<uint4*>(f.stage) + lane * NJ;
+  const int nj = (RT && !EDGE) ? r.nj : NJ;
+  uint4* chunk = reinterpret_cast<uint4*>(f.stage) + lane * nj;
 #pragma unroll 1
-  for (int j = 0; j < NJ; ++j) {
+  for (int j = 0; j < nj; ++j) {
     const int v = (j & ~7) | ((j & 7) ^ sw);
     uint4 w = chunk[v];
-    const int i0 = (lane * NJ + v) * 4 - r.mis;
+    const int i0 = (lane * nj + v) * 4 - r.mis;
     w.x = __float_as_uint(xform<true, EDGE>(__uint_as_float(w.x), i0, r));
     w.y = __float_as_uint(xform<true, EDGE>(__uint_as_float(w.y), i0 + 1, r));
     w.z = __float_as_uint(xform<true, EDGE>(__uint_as_float(w.z), i0 + 2, r));
@@ -1248,7 +1264,7 @@ __device__ __forceinline__ void hist_add(uint32_t* h, int b, float x) {
 // at a time, one per lane, with ballot prefix counts placing each lane's
 // candidates.  Returns the number of candidates, or -1 when there are more
 // than ROW_CAP.
-template <int DT, int NJ, bool XF, bool EDGE>
+template <int DT, int NJ, bool XF, bool EDGE, bool RT>
 __device__ __forceinline__ int collect_cands(const RowCtx& r, uint32_t flags, float tau,
                                              uint16_t* Qs, uint2* L) {
   constexpr int EPV = Elem<DT>::EPV;
@@ -1257,10 +1273,11 @@ __device__ __forceinline__ int collect_cands(const RowCtx& r, uint32_t flags, fl
   const int incl = (int)warp_inclusive_scan((uint32_t)nf);
   const int NF = __shfl_sync(FULL, incl, 31);
   {
+    const int nj = (RT && !EDGE) ? r.nj : NJ;
     int p = incl - nf;
     uint32_t fl = flags;
     while (fl) {
-      Qs[p++] = (uint16_t)(lane * NJ + __ffs(fl) - 1);
+      Qs[p++] = (uint16_t)(lane * nj + __ffs(fl) - 1);
       fl &= fl - 1;
     }
   }
@@ -1744,15 +1761,22 @@ __device__ void debug_masks(const void* p0, const RowCtx& r, float t, unsigned c
   __syncwarp();
 }
 
-// Outcomes of the templated front of the fast path.
-enum { FRONT_GENERAL = 0, FRONT_DONE = 1, FRONT_LIST = 2 };
+// Outcomes of the templated front of the fast path.  The FRONT_GEN_*
+// outcomes send the row to the general path, each for its own reason.
+enum {
+  FRONT_DONE = 1,
+  FRONT_LIST = 2,
+  FRONT_GEN_INF = 3,       // a raw +inf logit (rows selecting on raw values)
+  FRONT_GEN_TAU = 4,       // no usable threshold on the vector maxima
+  FRONT_GEN_OVERFLOW = 5,  // more than ROW_CAP candidates
+};
 
 // Fast path, up to the candidate list: scan, release of the stage, tau and
 // the collection.  FRONT_LIST leaves c candidates in f.list with the row
 // maximum Mx and the lower bound lo of their values (after the temperature);
-// FRONT_DONE sets `out`; FRONT_GENERAL sends the row to the general path
+// FRONT_DONE sets `out`; FRONT_GEN_* sends the row to the general path
 // (which reads the row from global memory).
-template <int DT, int NJ, bool XF, bool EDGE>
+template <int DT, int NJ, bool XF, bool EDGE, bool RT>
 __device__ int fast_front(const FastSpace& f, int k, bool use_top_p, const RowCtx& rc,
                           Releaser& rel, float& delta, RowOut& out, int& c_out, float& Mx_out,
                           float& lo_out) {
@@ -1760,13 +1784,13 @@ __device__ int fast_front(const FastSpace& f, int k, bool use_top_p, const RowCt
   float mx;
   if (XF && DT == Q3S_DTYPE_F32) {
     // f32 rows are transformed in the stage first; the scan is then plain.
-    xform_stage_f32<NJ, EDGE>(f, rc);
-    mx = scan_stage<DT, NJ, false, EDGE>(f, rc, vm);
+    xform_stage_f32<NJ, EDGE, RT>(f, rc);
+    mx = scan_stage<DT, NJ, false, EDGE, RT>(f, rc, vm);
   } else {
-    mx = scan_stage<DT, NJ, XF, EDGE>(f, rc, vm);
+    mx = scan_stage<DT, NJ, XF, EDGE, RT>(f, rc, vm);
   }
   release<DT>(rel);  // everything below reads the row from global memory
-  if (!XF && mx == __int_as_float(0x7f800000)) return FRONT_GENERAL;  // raw +inf
+  if (!XF && mx == __int_as_float(0x7f800000)) return FRONT_GEN_INF;  // raw +inf
   if (mx == neg_inf() || mx != mx) {
     out = {rc.sf >= 0 ? Q3S_STATUS_SUPPRESSION_NO_CANDIDATE : Q3S_STATUS_NO_CANDIDATE, 0u};
     return FRONT_DONE;
@@ -1778,7 +1802,7 @@ __device__ int fast_front(const FastSpace& f, int k, bool use_top_p, const RowCt
   }
   const int hi = k <= 128 ? max(2 * k, 64) : k + 96;
   float tau = mx;  // k == 1: the maximum and its ties
-  if (k > 1 && !find_tau(vm, mx, k, hi, delta, tau)) return FRONT_GENERAL;
+  if (k > 1 && !find_tau(vm, mx, k, hi, delta, tau)) return FRONT_GEN_TAU;
   // Raw-domain selection: lower tau until its image lies strictly below the
   // image of tau, so no element below the new tau can tie the k-th largest
   // x after the multiply.
@@ -1791,13 +1815,13 @@ __device__ int fast_front(const FastSpace& f, int k, bool use_top_p, const RowCt
       t2 = __fsub_rn(t2, fmaxf(fabsf(t2) * 3.814697265625e-06f, 1.1754944e-38f));
       ok = __fmul_rn(t2, rc.inv) < img;
     }
-    if (!ok) return FRONT_GENERAL;
+    if (!ok) return FRONT_GEN_TAU;
     tau = t2;
   }
   const uint32_t flags = chunk_flags(vm, tau);
-  const int c = collect_cands<DT, NJ, XF, EDGE>(rc, flags, tau,
+  const int c = collect_cands<DT, NJ, XF, EDGE, RT>(rc, flags, tau,
                                                 reinterpret_cast<uint16_t*>(f.Kb), f.list);
-  if (c < k) return FRONT_GENERAL;  // more than ROW_CAP candidates (or none: impossible)
+  if (c < k) return FRONT_GEN_OVERFLOW;  // more than ROW_CAP candidates (or none: impossible)
   c_out = c;
   Mx_out = Mx;
   lo_out = XF ? tau : __fmul_rn(tau, rc.inv);  // every candidate lies in [lo, Mx]
@@ -1870,7 +1894,7 @@ __device__ __forceinline__ int xband(float x, float Mx) {
 template <int NJ>
 __device__ __noinline__ unsigned long long nucleus_front(
     unsigned char* stage, uint2* list, uint32_t* hist, const uint32_t* bm, int n, int mis,
-    float inv, float pf, int use_pen, int sf, int allow, int edge) {
+    float inv, float pf, int use_pen, int sf, int allow, int edge, int nj) {
   const int lane = (int)lane_id();
   const uint32_t lt = lanemask_lt();
   float* row = reinterpret_cast<float*>(stage) + mis;  // element i at row[i]
@@ -1879,6 +1903,7 @@ __device__ __noinline__ unsigned long long nucleus_front(
   rc.n = n;
   rc.mis = mis;
   rc.Q = 0;
+  rc.nj = nj;
   rc.g16 = nullptr;
   rc.inv = inv;
   rc.pf = pf;
@@ -1887,14 +1912,14 @@ __device__ __noinline__ unsigned long long nucleus_front(
   rc.allow = allow;
   rc.bm = bm;
   const int sw = lane & 7;
-  float4* chunk = reinterpret_cast<float4*>(stage) + lane * NJ;
+  float4* chunk = reinterpret_cast<float4*>(stage) + lane * nj;
   // Mask and temperature in place (sampling.rs:608-631), and the maximum.
   float mx = neg_inf();
 #pragma unroll 1
-  for (int j = 0; j < NJ; ++j) {
+  for (int j = 0; j < nj; ++j) {
     const int v = (j & ~7) | ((j & 7) ^ sw);
     float4 w = chunk[v];
-    const int i0 = (lane * NJ + v) * 4 - mis;
+    const int i0 = (lane * nj + v) * 4 - mis;
     if (edge) {
       w.x = xform<true, true>(w.x, i0, rc);
       w.y = xform<true, true>(w.y, i0 + 1, rc);
@@ -1921,7 +1946,7 @@ __device__ __noinline__ unsigned long long nucleus_front(
   cnt[lane] = 0u;
   __syncwarp();
 #pragma unroll 1
-  for (int j = 0; j < NJ; ++j) {
+  for (int j = 0; j < nj; ++j) {
     const int v = (j & ~7) | ((j & 7) ^ sw);
     const float4 w = chunk[v];
     if (w.x >= cutoff) atomicAdd(&cnt[xband(w.x, Mx)], 1u);
@@ -1944,11 +1969,11 @@ __device__ __noinline__ unsigned long long nucleus_front(
   float xout = neg_inf();
   int c = 0;
 #pragma unroll 1
-  for (int j = 0; j < NJ; ++j) {
+  for (int j = 0; j < nj; ++j) {
     const int v = (j & ~7) | ((j & 7) ^ sw);
     const float4 w = chunk[v];
     const float x[4] = {w.x, w.y, w.z, w.w};
-    const int i0 = (lane * NJ + v) * 4 - mis;
+    const int i0 = (lane * nj + v) * 4 - mis;
     float e[4];
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
@@ -2062,10 +2087,13 @@ __device__ __noinline__ unsigned long long nucleus_finish(uint2* list, unsigned 
 // DBG: the launch fills the debug outputs (probs, masks).  Production
 // launches compile without that code, which would otherwise weigh on the
 // register allocation of the hot path.
-template <int DT, int NJ, bool DBG>
+// `path` receives the Q3S_PATH_* the row took (read by debug launches only).
+// RT: the launch's rows may be shorter than the kernel's chunk (mixed
+// vocabularies), see the dispatch below.
+template <int DT, int NJ, bool DBG, bool RT>
 __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const GenSpace& g,
                               const RowPlan& pl, int sf, int allow, const StageView& s,
-                              Releaser& rel, float& delta, const DebugRow& dbg_in) {
+                              Releaser& rel, float& delta, const DebugRow& dbg_in, int& path) {
   const DebugRow dbg{DBG ? dbg_in.masks : nullptr, DBG ? dbg_in.probs : nullptr};
   const uint32_t flags = pl.nf >> 16;
   const bool use_top_p = (flags & PF_TOP_P) != 0u;
@@ -2084,22 +2112,40 @@ __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const Gen
   const bool inv_ok = rc.inv > 0.0f && rc.inv < __int_as_float(0x7f800000);
   const bool fast = inv_ok && pl.k >= 1u && pl.k <= (uint32_t)FAST_MAX_K &&
                     pl.k < (uint32_t)s.n && s.Q <= 32 * NJ;
+  path = Q3S_PATH_GENERAL_RULES;
+  // A row is scanned without per-element index masks when it fills exactly
+  // 32 lane chunks: of NJ vectors, or, in a runtime-chunk launch (RT), of
+  // any multiple of 8 vectors below NJ (the 2048-entry code-predictor rows
+  // beside 3072-entry talker rows).  Both kinds then run one code path,
+  // which keeps the instruction cache to one copy of the scan.  Every other
+  // row is EDGE.
+  const bool aligned = s.mis == 0 && (s.n % Elem<DT>::EPV) == 0;
+  const bool exact = aligned && (RT ? ((s.Q & 255) == 0 && s.Q <= 32 * NJ) : s.Q == 32 * NJ);
+  rc.nj = exact ? (s.Q >> 5) : NJ;
   if (fast) {
     const bool xf = rc.use_pen || rc.sf >= 0;
-    const bool edge = s.mis != 0 || (s.n % Elem<DT>::EPV) != 0 || s.Q != 32 * NJ;
+    const bool edge = !exact;
     const int k = (int)pl.k;
     RowOut out;
     int c = 0;
     float Mx = 0.0f, lo = 0.0f;
     int fr;
     if (xf)
-      fr = edge ? fast_front<DT, NJ, true, true>(f, k, use_top_p, rc, rel, delta, out, c, Mx, lo)
-                : fast_front<DT, NJ, true, false>(f, k, use_top_p, rc, rel, delta, out, c, Mx, lo);
+      fr = edge ? fast_front<DT, NJ, true, true, RT>(f, k, use_top_p, rc, rel, delta, out, c, Mx, lo)
+                : fast_front<DT, NJ, true, false, RT>(f, k, use_top_p, rc, rel, delta, out, c, Mx,
+                                                      lo);
     else
-      fr = edge ? fast_front<DT, NJ, false, true>(f, k, use_top_p, rc, rel, delta, out, c, Mx, lo)
-                : fast_front<DT, NJ, false, false>(f, k, use_top_p, rc, rel, delta, out, c, Mx,
-                                                   lo);
-    if (fr == FRONT_DONE) return out;
+      fr = edge ? fast_front<DT, NJ, false, true, RT>(f, k, use_top_p, rc, rel, delta, out, c, Mx,
+                                                      lo)
+                : fast_front<DT, NJ, false, false, RT>(f, k, use_top_p, rc, rel, delta, out, c, Mx,
+                                                       lo);
+    if (fr == FRONT_DONE) {
+      path = Q3S_PATH_FRONT_DONE;
+      return out;
+    }
+    path = fr == FRONT_GEN_INF ? Q3S_PATH_GENERAL_INF
+           : fr == FRONT_GEN_TAU ? Q3S_PATH_GENERAL_TAU
+                                 : Q3S_PATH_GENERAL_OVERFLOW;
     if (fr == FRONT_LIST) {
       float* tsm = reinterpret_cast<float*>(f.hist);
       float* Bb = reinterpret_cast<float*>(f.Kb);
@@ -2112,7 +2158,11 @@ __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const Gen
                              dbg.masks, dbg.probs);
       }
       out = {(int)(r >> 32), (uint32_t)r};
-      if (out.status == WIDE_GENERAL) goto general;
+      path = use_top_p ? Q3S_PATH_TOPK_TOPP : Q3S_PATH_TOPK;
+      if (out.status == WIDE_GENERAL) {
+        path = Q3S_PATH_GENERAL_WIDE;
+        goto general;
+      }
       if (dbg.masks) {
         __syncwarp();
         if (xf)
@@ -2127,16 +2177,16 @@ general:
   if constexpr (DT == Q3S_DTYPE_F32) {
     // Top-p without top-k: the nucleus from the stage-resident row.
     if (use_top_p && inv_ok && (pl.k == 0u || pl.k >= (uint32_t)s.n) && s.Q <= 32 * NJ) {
-      const int edge = (s.mis != 0 || (s.n % Elem<DT>::EPV) != 0 || s.Q != 32 * NJ) ? 1 : 0;
       unsigned long long r =
           nucleus_front<NJ>(f.stage, f.list, f.hist, f.bm, s.n, s.mis, rc.inv, rc.pf,
-                            rc.use_pen ? 1 : 0, rc.sf, rc.allow, edge);
+                            rc.use_pen ? 1 : 0, rc.sf, rc.allow, exact ? 0 : 1, rc.nj);
       release<DT>(rel);
       if ((int)(r >> 32) == Q3S_STATUS_OK) {
         r = nucleus_finish(f.list, f.Kb, f.hist, (int)(uint32_t)r, s.n, pl.top_p, u, dbg.masks,
                            dbg.probs);
       }
       const RowOut out{(int)(r >> 32), (uint32_t)r};
+      path = out.status == WIDE_GENERAL ? Q3S_PATH_GENERAL_NUCLEUS : Q3S_PATH_NUCLEUS;
       if (out.status != WIDE_GENERAL) {
         if (dbg.masks && out.status == Q3S_STATUS_OK) {
           __syncwarp();
@@ -2158,7 +2208,7 @@ general:
   return {(int)(r >> 32), (uint32_t)r};
 }
 
-template <int DT, int NJ, bool DBG>
+template <int DT, int NJ, bool DBG, bool RT>
 __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int es = Elem<DT>::BYTES;
@@ -2207,6 +2257,7 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
     t = __shfl_sync(FULL, t, 0);
     const long long row = blockIdx.x + (long long)t * G;
     if (row >= a.num_rows) break;
+    const long long clk0 = DBG ? clock64() : 0;
     const int slot = (int)(t % RING);
     const uint32_t gen = t / RING;
     f.stage = ring + slot * sbytes;
@@ -2252,18 +2303,24 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
     }
     if (lane == 0) ctl->consumed[slot] = gen + 1u;
     RowOut out{st, 0u};
+    int path = Q3S_PATH_INVALID;
     if (st == Q3S_STATUS_OK) {
       const StageView s = complete_stage<DT>(a, row, n, f.stage);
       if (!(pflags & PF_DO_SAMPLE)) {
         out = greedy_stage<DT>(f, s, sf, allow);
+        path = Q3S_PATH_GREEDY;
       } else {
-        out = sampled_row<DT, NJ, DBG>(a, f, g, pl, sf, allow, s, rel, delta, dbg);
+        out = sampled_row<DT, NJ, DBG, RT>(a, f, g, pl, sf, allow, s, rel, delta, dbg, path);
       }
     }
     release<DT>(rel);
     if (lane == 0) {
       a.tokens[row] = out.token;
       a.status[row] = (unsigned char)out.status;
+      if (DBG && a.path_stats) {
+        atomicAdd(&a.path_stats[path], 1ull);
+        atomicAdd(&a.path_stats[Q3S_PATH_COUNT + path], (unsigned long long)(clock64() - clk0));
+      }
     }
     __syncwarp();
   }
@@ -2342,20 +2399,29 @@ cudaError_t ensure_smem(K kernel, std::atomic<int>* set, size_t smem) {
   return e;
 }
 
-template <int DT, int NJ, bool DBG>
+template <int DT, int NJ, bool DBG, bool RT>
 cudaError_t launch_dbg(const KernelArgs& a, int grid, int warps, cudaStream_t stream) {
   static std::atomic<int> smem_set[MAX_DEVICES];
   const size_t smem = block_smem(a.vcap, Elem<DT>::BYTES, warps);
-  cudaError_t e = ensure_smem(sample_kernel<DT, NJ, DBG>, smem_set, smem);
+  cudaError_t e = ensure_smem(sample_kernel<DT, NJ, DBG, RT>, smem_set, smem);
   if (e != cudaSuccess) return e;
-  sample_kernel<DT, NJ, DBG><<<grid, warps * 32, smem, stream>>>(a);
+  sample_kernel<DT, NJ, DBG, RT><<<grid, warps * 32, smem, stream>>>(a);
   return cudaGetLastError();
 }
 
+// Launches with per-row vocabularies run the runtime-chunk kernel when the
+// kernel's chunk holds two or more groups of 8 vectors (a shorter exact row
+// is then possible); all other launches keep the fixed-chunk code.
 template <int DT, int NJ>
 cudaError_t launch_t(const KernelArgs& a, int grid, int warps, cudaStream_t stream) {
-  if (a.probs || a.masks) return launch_dbg<DT, NJ, true>(a, grid, warps, stream);
-  return launch_dbg<DT, NJ, false>(a, grid, warps, stream);
+  const bool dbg = a.probs || a.masks || a.path_stats;
+  if constexpr (NJ >= 16) {
+    if (a.row_vocab)
+      return dbg ? launch_dbg<DT, NJ, true, true>(a, grid, warps, stream)
+                 : launch_dbg<DT, NJ, false, true>(a, grid, warps, stream);
+  }
+  return dbg ? launch_dbg<DT, NJ, true, false>(a, grid, warps, stream)
+             : launch_dbg<DT, NJ, false, false>(a, grid, warps, stream);
 }
 
 }  // namespace

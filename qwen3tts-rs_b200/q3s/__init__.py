@@ -119,7 +119,13 @@ EXPORTED_SYMBOLS = (
     "q3s_sampler_destroy", "q3s_sampler_subsequence_counter",
     "q3s_sampler_set_subsequence_counter", "q3s_sampler_get_diagnostics",
     "q3s_sampler_sample_with_mode", "q3s_sampler_sample", "q3s_sample_batch_static",
-    "q3s_embed_sum", "q3s_context_set_test_hooks",
+    "q3s_embed_sum", "q3s_context_set_test_hooks", "q3s_context_set_path_stats",
+)
+
+# Row paths of the sampling kernel (Q3S_PATH_* of include/q3s_sampler.h).
+PATH_NAMES = (
+    "invalid", "greedy", "topk", "topk_topp", "front_done", "nucleus", "general_rules",
+    "general_inf", "general_tau", "general_overflow", "general_wide", "general_nucleus",
 )
 
 _lib = None
@@ -149,6 +155,7 @@ def load(path: Optional[os.PathLike] = None):
     L.q3s_context_destroy.argtypes = [ctypes.c_void_p]
     L.q3s_context_destroy.restype = None
     L.q3s_context_set_test_hooks.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int32]
+    L.q3s_context_set_path_stats.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
     L.q3s_sample_batch.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Batch), ctypes.c_void_p]
     L.q3s_sample_batch_static.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Batch),
                                           ctypes.c_void_p]
@@ -235,6 +242,18 @@ class Context:
         _check(load().q3s_context_set_test_hooks(self._h, int(stage_wait_ns),
                                                  1 if hold_refill else 0),
                "q3s_context_set_test_hooks")
+
+    def set_path_stats(self, stats) -> None:
+        """Diagnostics (q3s_context_set_path_stats): `stats` is an int64
+        device tensor of 2 * len(PATH_NAMES) entries that this context's
+        batched launches accumulate into (rows, then warp cycles, per path),
+        or None to stop."""
+        if stats is not None and (stats.numel() < 2 * len(PATH_NAMES) or
+                                  stats.element_size() != 8 or not stats.is_contiguous()):
+            raise ValueError("path stats need a contiguous 8-byte tensor of 2 * PATH_COUNT")
+        _check(load().q3s_context_set_path_stats(self._h, None if stats is None
+                                                 else stats.data_ptr()),
+               "q3s_context_set_path_stats")
 
     def close(self) -> None:
         if self._h:
@@ -628,3 +647,12 @@ class Sampler:
     def sample(self, logits, options, suppress_from=None, allow_token=None, history=()) -> int:
         return self.sample_with_mode(logits, options, options.temperature > 0.0, suppress_from,
                                      allow_token, history)
+
+
+def path_report(stats) -> dict:
+    """{path name: {"rows", "cycles_per_row"}} of the paths a path-stats
+    tensor saw (Context.set_path_stats)."""
+    v = [int(x) for x in stats.cpu().tolist()]
+    P = len(PATH_NAMES)
+    return {name: {"rows": v[i], "cycles_per_row": v[P + i] / v[i]}
+            for i, name in enumerate(PATH_NAMES) if v[i]}

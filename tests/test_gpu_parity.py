@@ -462,13 +462,27 @@ def test_bounded_stage_wait_gives_up_and_context_stays_usable():
     np.testing.assert_array_equal(t2.cpu().numpy().view(np.uint32), ref["tokens"])
 
 
+def _general_rows(seed):
+    """The 1024-row talker batch with top-p 1: top-k off and no nucleus, so
+    every row takes the general path and its per-warp global workspace."""
+    w = workloads.talker_batch(DEV, rows=1024, seed=seed)
+    w.params["top_p"] = 1.0
+    return w
+
+
 def test_general_path_rows_on_two_streams_of_one_context():
-    """Rows on the general path (top-k off, top-p 0.8, penalties: the
-    1024-row talker batch) use the per-stream workspace; two streams of one
-    context run them concurrently and both match the oracle."""
+    """Rows on the general path use the per-stream workspace; two streams of
+    one context run them concurrently and both match the oracle."""
     ctx = q3s.Context(0)
-    ws = [workloads.talker_batch(DEV, rows=1024, seed=2),
-          workloads.talker_batch(DEV, rows=1024, seed=12)]
+    ws = [_general_rows(2), _general_rows(12)]
+    stats = torch.zeros(2 * len(q3s.PATH_NAMES), dtype=torch.int64, device=DEV)
+    a = ws[0].device_args(DEV)
+    ctx.set_path_stats(stats)
+    q3s.sample_batch(ws[0].logits, a.pop("params"), a.pop("seeds"), a.pop("subseqs"), ctx=ctx,
+                     **a)
+    torch.cuda.synchronize()
+    ctx.set_path_stats(None)
+    assert q3s.path_report(stats) .keys() == {"general_rules"}
     refs = [oracle_tokens(w) for w in ws]
     streams = [torch.cuda.Stream(DEV), torch.cuda.Stream(DEV)]
     args = []
@@ -488,3 +502,38 @@ def test_general_path_rows_on_two_streams_of_one_context():
         t, st = outs[i]
         np.testing.assert_array_equal(st.cpu().numpy(), refs[i]["status"])
         np.testing.assert_array_equal(t.cpu().numpy().view(np.uint32), refs[i]["tokens"])
+
+
+def test_path_stats_count_every_row_once():
+    """q3s_context_set_path_stats: every row of a launch is counted once, on
+    the path its parameters lead to, and the results equal a launch without
+    the counters."""
+    ctx = q3s.Context(0)
+    R = 2048
+    w = workloads.bandwidth(DEV, rows=R, top_k=50)
+    params = np.repeat(q3s.make_params(1, top_k=50), R)
+    params["do_sample"][:256] = 0                       # greedy
+    params["temperature"][256:320] = -1.0               # invalid temperature
+    params["top_k"][320:512] = 0                        # k off, top-p 1: general path
+    params["top_k"][512:768] = 0                        # k off, top-p 0.8, sharp: nucleus
+    params["top_p"][512:768] = 0.8
+    params["temperature"][512:768] = 0.25
+    params["top_p"][768:1024] = 0.9                     # top-k then top-p
+    w.params = params
+    a = w.device_args(DEV)
+    p, s, u = a.pop("params"), a.pop("seeds"), a.pop("subseqs")
+    t0, st0 = q3s.sample_batch(w.logits, p, s, u, ctx=ctx)
+    stats = torch.zeros(2 * len(q3s.PATH_NAMES), dtype=torch.int64, device=DEV)
+    ctx.set_path_stats(stats)
+    t1, st1 = q3s.sample_batch(w.logits, p, s, u, ctx=ctx)
+    torch.cuda.synchronize()
+    ctx.set_path_stats(None)
+    rep = q3s.path_report(stats)
+    assert {k: v["rows"] for k, v in rep.items()} == {
+        "greedy": 256, "invalid": 64, "general_rules": 192, "nucleus": 256, "topk_topp": 256,
+        "topk": R - 1024}
+    assert all(v["cycles_per_row"] > 0 for v in rep.values())
+    assert torch.equal(t0, t1) and torch.equal(st0, st1)
+    ref = oracle_tokens(w)
+    np.testing.assert_array_equal(st1.cpu().numpy(), ref["status"])
+    np.testing.assert_array_equal(t1.cpu().numpy().view(np.uint32), ref["tokens"])
