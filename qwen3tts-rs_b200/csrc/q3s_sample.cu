@@ -1260,13 +1260,15 @@ __device__ __forceinline__ void hist_add(uint32_t* h, int b, float x) {
 // The candidates {x >= tau} of the flagged vectors, in vocabulary order, as
 // (x after the temperature, index) into L.  The flagged vectors are first
 // listed warp-wide (lane-major = vocabulary order) in Qs, then read back
-// from global memory (L2: the row was staged moments ago) and processed 32
-// at a time, one per lane, with ballot prefix counts placing each lane's
-// candidates.  Returns the number of candidates, or -1 when there are more
+// and processed 32 at a time, one per lane, with ballot prefix counts
+// placing each lane's candidates.  STAGED: the vectors come from the stage,
+// which already holds x (f32 rows transformed in place); otherwise from
+// global memory (L2: the row was staged moments ago), transformed again
+// when XF.  Returns the number of candidates, or -1 when there are more
 // than ROW_CAP.
-template <int DT, int NJ, bool XF, bool EDGE, bool RT>
+template <int DT, int NJ, bool XF, bool EDGE, bool RT, bool STAGED>
 __device__ __forceinline__ int collect_cands(const RowCtx& r, uint32_t flags, float tau,
-                                             uint16_t* Qs, uint2* L) {
+                                             uint16_t* Qs, uint2* L, const uint4* stage) {
   constexpr int EPV = Elem<DT>::EPV;
   const int lane = (int)lane_id();
   const int nf = __popc(flags);
@@ -1285,14 +1287,15 @@ __device__ __forceinline__ int collect_cands(const RowCtx& r, uint32_t flags, fl
   const uint32_t lt = lanemask_lt();
   int base = 0;
   // Each lane's next vector is loaded one iteration ahead.
+  auto load = [&](int q) { return STAGED ? stage[q] : __ldg(r.g16 + q); };
   int qn = lane < NF ? (int)Qs[lane] : -1;
-  uint4 wn = qn >= 0 ? __ldg(r.g16 + qn) : make_uint4(0u, 0u, 0u, 0u);
+  uint4 wn = qn >= 0 ? load(qn) : make_uint4(0u, 0u, 0u, 0u);
   for (int i0 = 0; i0 < NF; i0 += 32) {
     const int q = qn;
     const uint4 w = wn;
     const int inext = i0 + 32 + lane;
     qn = inext < NF ? (int)Qs[inext] : -1;
-    if (qn >= 0) wn = __ldg(r.g16 + qn);
+    if (qn >= 0) wn = load(qn);
     float x[EPV];
     uint32_t bits = 0;
     if (q >= 0) {
@@ -1300,7 +1303,7 @@ __device__ __forceinline__ int collect_cands(const RowCtx& r, uint32_t flags, fl
       unpack_vec<DT>(w, e);
 #pragma unroll
       for (int c = 0; c < EPV; ++c) {
-        x[c] = xform<XF, EDGE>(e[c], q * EPV + c - r.mis, r);
+        x[c] = STAGED ? e[c] : xform<XF, EDGE>(e[c], q * EPV + c - r.mis, r);
         bits |= (x[c] >= tau ? 1u : 0u) << c;
       }
     }
@@ -1317,7 +1320,7 @@ __device__ __forceinline__ int collect_cands(const RowCtx& r, uint32_t flags, fl
 #pragma unroll
     for (int c = 0; c < EPV; ++c)
       if (bits & (1u << c))
-        L[o++] = make_uint2(__float_as_uint(XF ? x[c] : __fmul_rn(x[c], r.inv)),
+        L[o++] = make_uint2(__float_as_uint((XF || STAGED) ? x[c] : __fmul_rn(x[c], r.inv)),
                             (uint32_t)(q * EPV + c - r.mis));
     base += tot;
   }
@@ -1656,20 +1659,75 @@ __device__ __forceinline__ unsigned long long finish_topk_hist(
 // then takes the general path).
 constexpr int WIDE_GENERAL = 0x7E;
 
+// The nucleus walk of sampling.rs:680-697 over the survivors L[0..ns) in
+// vocabulary order, ns <= 32 R (one instantiation, R = 8: a second one
+// costs more in instruction-cache misses than its shorter sort saves): each survivor within 16 of the maximum has
+// p = Bb[j] * inv_total (Bb[j] = exp(x - Mx)); the reference visits them by
+// (p desc, index asc) and keeps the positions before the first position > 0
+// whose preceding cumulative reaches top_p.  Here the p values alone are
+// sorted (32-bit keys ~bits(p): ascending key = descending p; ties keep equal
+// p, which is all the cumulative needs), one lane chains their prefix sums
+// into P (32 R floats), and the first position q >= 1 with P[q - 1] >= top_p
+// is found in parallel.  Returns J, the nucleus size; kJ is the key of its
+// last member and gt the number of survivors with a smaller key (larger p):
+// the nucleus is every survivor with key < kJ plus the J - gt survivors of
+// key kJ with the smallest indices.
+template <int R>
+__device__ __forceinline__ int topp_walk(const uint2* L, const float* Bb, int ns, float cutoff,
+                                         float inv_total, float top_p, float* P, uint32_t& kJ,
+                                         int& gt) {
+  const int lane = (int)lane_id();
+  uint32_t v[R];
+  int cnt = 0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int j = lane * R + r;
+    v[r] = 0xFFFFFFFFu;
+    if (j < ns && ex(L[j]) >= cutoff) {
+      v[r] = ~__float_as_uint(__fmul_rn(Bb[j], inv_total));
+      ++cnt;
+    }
+  }
+  const int m = (int)__reduce_add_sync(FULL, (unsigned)cnt);
+  bitonic<R>(v);
+#pragma unroll
+  for (int r = 0; r < R; ++r) P[lane * R + r] = v[r] != 0xFFFFFFFFu ? __uint_as_float(~v[r]) : 0.0f;
+  __syncwarp();
+  chain_smem<true>(P, m);
+  int first = m;
+  for (int q = 1 + lane; q < m; q += 32) {
+    if (P[q - 1] >= top_p) {
+      first = q;
+      break;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) first = min(first, __shfl_xor_sync(FULL, first, o));
+  const int J = first;  // >= 1: the row maximum is always within 16 of itself
+  uint32_t mine = 0u;
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+    if (lane * R + r == J - 1) mine = v[r];
+  kJ = __shfl_sync(FULL, mine, (J - 1) / R);
+  int g = 0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) g += v[r] < kJ ? 1 : 0;
+  gt = (int)__reduce_add_sync(FULL, (unsigned)g);
+  __syncwarp();
+  return J;
+}
+
 // Finishes a top-p row from its candidates L[0..c) in vocabulary order,
 // k <= c <= ROW_CAP (sampling.rs:654-729): the exact k-th largest t and the
 // survivors x >= t as in finish_topk_hist; the top-p denominator, the
 // sequential f32 sum of exp(x - Mx) over the survivors in vocabulary order
 // (every other entry is masked, an exact zero of the reference's sum); the
-// survivors within 16 of the maximum sorted by (p desc, index asc), p =
-// exp(x - Mx) * inv_total, in one register sort of 64-bit keys; one lane
-// walks the cumulative; the nucleus is compacted in place (vocabulary order)
-// and drawn by draw_tail with its own maximum.  More than 256 survivors:
-// WIDE_GENERAL.  Bb and Kb alias (the terms are read before the keys are
-// stored); h: 8 words for the nucleus marks.
+// nucleus by topp_walk, compacted in place (vocabulary order) and drawn by
+// draw_tail with its own maximum.  More than 256 survivors: WIDE_GENERAL.
+// Bb: the exp terms in [0, 256 + 8), the walk's prefix sums in [256, 512).
 __device__ __forceinline__ unsigned long long finish_topp_hist(
     uint2* L, int c, int k, int n, float Mx, float lo, float u, float top_p, float* Bb,
-    unsigned long long* Kb, uint32_t* h, float* tsm, unsigned char* masks, float* probs) {
+    uint32_t* h, float* tsm, unsigned char* masks, float* probs) {
   const int lane = (int)lane_id();
   const uint32_t lt = lanemask_lt();
   const float t = kth_largest(L, c, k, Mx, lo, Bb, h);
@@ -1684,58 +1742,25 @@ __device__ __forceinline__ unsigned long long finish_topp_hist(
   if (!is_finite(total) || total <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
   const float inv_total = __fdiv_rn(1.0f, total);
   const float cutoff = __fsub_rn(Mx, 16.0f);
-  // (p desc, index asc) over the entries within 16 of the maximum
-  // (sampling.rs:680-689); low bits: index, then list position.
-  unsigned long long v[8];
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const int j = lane * 8 + r;
-    v[r] = ~0ull;
-    if (j < ns) {
-      const uint2 en = L[j];
-      if (ex(en) >= cutoff) {
-        const float p = __fmul_rn(Bb[j], inv_total);
-        v[r] = ((unsigned long long)(~__float_as_uint(p)) << 32) | (en.y << 16) | (uint32_t)j;
-      }
-    }
-  }
-  __syncwarp();
-  bitonic<8>(v);
-#pragma unroll
-  for (int r = 0; r < 8; ++r) Kb[lane * 8 + r] = v[r];
-  __syncwarp();
-  // The nucleus: positions before the first position > 0 whose preceding
-  // cumulative reaches top_p (sampling.rs:690-697).
-  int J = 0;
-  if (lane == 0) {
-    float cum = 0.0f;
-    for (int q = 0; q < 256; ++q) {
-      const unsigned long long key = Kb[q];
-      if (key == ~0ull) break;
-      if (q > 0 && cum >= top_p) break;
-      cum = __fadd_rn(cum, __uint_as_float(~(uint32_t)(key >> 32)));
-      J = q + 1;
-    }
-  }
-  J = __shfl_sync(FULL, J, 0);
-  if (lane < 8) h[lane] = 0u;
-  __syncwarp();
-  for (int q = lane; q < J; q += 32) {
-    const uint32_t j = (uint32_t)Kb[q] & 0xFFFFu;
-    atomicOr(&h[j >> 5], 1u << (j & 31));
-  }
-  __syncwarp();
+  uint32_t kJ;
+  int gt;
+  const int J = topp_walk<8>(L, Bb, ns, cutoff, inv_total, top_p, Bb + 256, kJ, gt);
+  const int need = J - gt;  // members of key kJ, by index
   // Compact the nucleus in place (vocabulary order kept) and take its maximum.
-  int n2 = 0;
+  int n2 = 0, ties = 0;
   float m2 = neg_inf();
   for (int j0 = 0; j0 < ns; j0 += 32) {
     const int j = j0 + lane;
-    const bool keep = j < ns && ((h[j >> 5] >> (j & 31)) & 1u);
     uint2 en = make_uint2(0u, 0u);
-    if (keep) {
+    uint32_t key = 0xFFFFFFFFu;
+    if (j < ns) {
       en = L[j];
-      m2 = fmaxf(m2, ex(en));
+      if (ex(en) >= cutoff) key = ~__float_as_uint(__fmul_rn(Bb[j], inv_total));
     }
+    const unsigned tb = __ballot_sync(FULL, key == kJ);
+    const bool keep = key < kJ || (key == kJ && ties + __popc(tb & lt) < need);
+    ties += __popc(tb);
+    if (keep) m2 = fmaxf(m2, ex(en));
     const unsigned bb = __ballot_sync(FULL, keep);
     if (keep) L[n2 + __popc(bb & lt)] = en;
     n2 += __popc(bb);
@@ -1780,16 +1805,20 @@ template <int DT, int NJ, bool XF, bool EDGE, bool RT>
 __device__ int fast_front(const FastSpace& f, int k, bool use_top_p, const RowCtx& rc,
                           Releaser& rel, float& delta, RowOut& out, int& c_out, float& Mx_out,
                           float& lo_out) {
+  // f32 rows with a transform hold x in their stage after the in-place
+  // transform: their candidates are collected from it, and the stage is
+  // released after the collection instead of after the scan.
+  constexpr bool STAGED = XF && DT == Q3S_DTYPE_F32;
   float vm[NJ];
   float mx;
-  if (XF && DT == Q3S_DTYPE_F32) {
+  if (STAGED) {
     // f32 rows are transformed in the stage first; the scan is then plain.
     xform_stage_f32<NJ, EDGE, RT>(f, rc);
     mx = scan_stage<DT, NJ, false, EDGE, RT>(f, rc, vm);
   } else {
     mx = scan_stage<DT, NJ, XF, EDGE, RT>(f, rc, vm);
   }
-  release<DT>(rel);  // everything below reads the row from global memory
+  if (!STAGED) release<DT>(rel);  // everything below reads the row from global memory
   if (!XF && mx == __int_as_float(0x7f800000)) return FRONT_GEN_INF;  // raw +inf
   if (mx == neg_inf() || mx != mx) {
     out = {rc.sf >= 0 ? Q3S_STATUS_SUPPRESSION_NO_CANDIDATE : Q3S_STATUS_NO_CANDIDATE, 0u};
@@ -1819,8 +1848,10 @@ __device__ int fast_front(const FastSpace& f, int k, bool use_top_p, const RowCt
     tau = t2;
   }
   const uint32_t flags = chunk_flags(vm, tau);
-  const int c = collect_cands<DT, NJ, XF, EDGE, RT>(rc, flags, tau,
-                                                reinterpret_cast<uint16_t*>(f.Kb), f.list);
+  const int c = collect_cands<DT, NJ, XF, EDGE, RT, STAGED>(
+      rc, flags, tau, reinterpret_cast<uint16_t*>(f.Kb), f.list,
+      reinterpret_cast<const uint4*>(f.stage));
+  if (STAGED) release<DT>(rel);
   if (c < k) return FRONT_GEN_OVERFLOW;  // more than ROW_CAP candidates (or none: impossible)
   c_out = c;
   Mx_out = Mx;
@@ -2154,7 +2185,7 @@ __device__ RowOut sampled_row(const KernelArgs& a, const FastSpace& f, const Gen
         r = finish_topk_hist(f.list, c, k, s.n, Mx, lo, u, Bb, f.hist + 16, tsm, dbg.masks,
                              dbg.probs);
       } else {
-        r = finish_topp_hist(f.list, c, k, s.n, Mx, lo, u, pl.top_p, Bb, f.Kb, f.hist + 16, tsm,
+        r = finish_topp_hist(f.list, c, k, s.n, Mx, lo, u, pl.top_p, Bb, f.hist + 16, tsm,
                              dbg.masks, dbg.probs);
       }
       out = {(int)(r >> 32), (uint32_t)r};
