@@ -381,23 +381,40 @@ __device__ __forceinline__ bool load_plan(const RowPlan* slot, uint32_t ticket, 
 }
 
 // The history bitmap of a row (sampling.rs:732-773: every id < n of the
-// history marks its entry once): bm[0 .. ceil(n/32)) cleared, then one bit
-// per id.  The ids are read as 16-byte vectors of 8, four vectors per lane in
-// flight (1024 ids per round trip of the warp), plus the unaligned head and
-// tail one id per lane; vector slots past the end read as 0xFFFF, which no
-// row's vocabulary reaches.
+// history marks its entry once): bm[0 .. ceil(n/32)) = one bit per id.  The
+// ids are read as 16-byte vectors of 8, four vectors per lane in flight (1024
+// ids per round trip of the warp), plus the unaligned head and tail one id
+// per lane; vector slots past the end read as 0xFFFF, which no row's
+// vocabulary reaches.  Lanes whose ids share a bitmap word would serialise on
+// an atomic OR, so histories longer than 64 ids are marked with plain byte
+// stores into a byte map `bytes` (32 * ceil(n/32) bytes, 16-byte aligned; an
+// id listed twice stores the same 1), which is then packed into bm, four
+// bytes of 0/1 at a time by one multiply: bytes b0..b3 of x land on bits
+// 24..27 of x * 0x01020408 (each byte lands on distinct bits, so nothing
+// carries).
 __device__ __forceinline__ void mark_id(uint32_t* bm, uint32_t id, int n) {
   if ((int)id < n) atomicOr(&bm[id >> 5], 1u << (id & 31));
 }
 
-__device__ __noinline__ void fill_history(const unsigned short* h, long long cnt, int n,
-                                          uint32_t* bm) {
+__device__ __forceinline__ void mark_byte(unsigned char* bytes, uint32_t id, int n) {
+  if ((int)id < n) bytes[id] = 1;
+}
+
+__device__ __forceinline__ uint32_t pack_bytes4(uint32_t x) { return (x * 0x01020408u) >> 24; }
+
+template <bool BYTES>
+__device__ __forceinline__ void mark_ids(const unsigned short* h, long long cnt, int n,
+                                         uint32_t* bm, unsigned char* bytes) {
   const int lane = (int)lane_id();
-  for (int w = lane; w < ((n + 31) >> 5); w += 32) bm[w] = 0u;
-  __syncwarp();
+  auto mark = [&](uint32_t id) {
+    if (BYTES)
+      mark_byte(bytes, id, n);
+    else
+      mark_id(bm, id, n);
+  };
   long long head = (long long)(((16u - (uint32_t)(reinterpret_cast<uintptr_t>(h) & 15u)) & 15u) >> 1);
   if (head > cnt) head = cnt;
-  if (lane < head) mark_id(bm, __ldg(h + lane), n);
+  if (lane < head) mark(__ldg(h + lane));
   const uint4* v = reinterpret_cast<const uint4*>(h + head);
   const long long nv = (cnt - head) >> 3;
   for (long long q0 = 0; q0 < nv; q0 += 128) {
@@ -412,12 +429,36 @@ __device__ __noinline__ void fill_history(const unsigned short* h, long long cnt
       const uint32_t ws[4] = {w[r].x, w[r].y, w[r].z, w[r].w};
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
-        mark_id(bm, ws[t] & 0xFFFFu, n);
-        mark_id(bm, ws[t] >> 16, n);
+        mark(ws[t] & 0xFFFFu);
+        mark(ws[t] >> 16);
       }
     }
   }
-  for (long long t = head + nv * 8 + lane; t < cnt; t += 32) mark_id(bm, __ldg(h + t), n);
+  for (long long t = head + nv * 8 + lane; t < cnt; t += 32) mark(__ldg(h + t));
+}
+
+__device__ __noinline__ void fill_history(const unsigned short* h, long long cnt, int n,
+                                          uint32_t* bm, unsigned char* bytes) {
+  const int lane = (int)lane_id();
+  const int W = (n + 31) >> 5;
+  if (cnt <= 64) {
+    for (int w = lane; w < W; w += 32) bm[w] = 0u;
+    __syncwarp();
+    mark_ids<false>(h, cnt, n, bm, bytes);
+    __syncwarp();
+    return;
+  }
+  uint4* B4 = reinterpret_cast<uint4*>(bytes);
+  for (int q = lane; q < 2 * W; q += 32) B4[q] = make_uint4(0u, 0u, 0u, 0u);
+  __syncwarp();
+  mark_ids<true>(h, cnt, n, bm, bytes);
+  __syncwarp();
+  for (int w = lane; w < W; w += 32) {
+    const uint4 a = B4[2 * w], b = B4[2 * w + 1];
+    bm[w] = pack_bytes4(a.x) | (pack_bytes4(a.y) << 4) | (pack_bytes4(a.z) << 8) |
+            (pack_bytes4(a.w) << 12) | (pack_bytes4(b.x) << 16) | (pack_bytes4(b.y) << 20) |
+            (pack_bytes4(b.z) << 24) | (pack_bytes4(b.w) << 28);
+  }
   __syncwarp();
 }
 
@@ -2318,7 +2359,7 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
     // stage copy may still be in flight).
     if (st == Q3S_STATUS_OK && (pflags & PF_USE_PEN)) {
       const long long h0 = a.history_offsets[row], h1 = a.history_offsets[row + 1];
-      fill_history(a.history + h0, h1 - h0, n, f.bm);
+      fill_history(a.history + h0, h1 - h0, n, f.bm, reinterpret_cast<unsigned char*>(f.list));
     }
     const bool ready = wait_stage(ctl, slot, gen, a.wait_ns);
     if (!__all_sync(FULL, ready)) {
