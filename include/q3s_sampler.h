@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define Q3S_ABI_VERSION 1
+#define Q3S_ABI_VERSION 2 /* 2: q3s_batch.history_ends appended */
 
 /* ---- return codes of API calls ------------------------------------------ */
 #define Q3S_OK 0
@@ -55,6 +55,7 @@ extern "C" {
 #define Q3S_STATUS_INVALID_DENOMINATOR 6
 #define Q3S_STATUS_UNSUPPORTED 7 /* vocabulary larger than Q3S_MAX_VOCAB */
 #define Q3S_STATUS_INVALID_CODE 8 /* q3s_embed_sum: a code outside its codebook (row zeroed) */
+#define Q3S_STATUS_HISTORY_FULL 9 /* q3s_commit_rows: no room to append the sampled c0 id */
 #define Q3S_STATUS_NOT_RUN 255   /* row was never reached (internal error) */
 
 /* Largest vocabulary one row may have (the codec vocabularies are 3072 and 2048). */
@@ -98,8 +99,10 @@ typedef struct q3s_row_params {
  * row_offsets is NULL) and hold row_vocab[r] (or vocab) elements.  Its
  * parameters are params[r*params_stride] (params_stride 0 broadcasts one
  * struct).  Its history is history[history_offsets[r] .. history_offsets[r+1])
- * (no history when history_offsets is NULL).  Its Philox key/counter are
- * seeds[r] / subseqs[r]. */
+ * (no history when history_offsets is NULL), or
+ * history[history_offsets[r] .. history_ends[r]) when history_ends is set
+ * (per-row ranges that need not abut: fixed-capacity per-session slots).
+ * Its Philox key/counter are seeds[r] / subseqs[r]. */
 typedef struct q3s_batch {
   const void* logits;
   int32_t dtype;
@@ -121,6 +124,7 @@ typedef struct q3s_batch {
   float* probs;                   /* out [num_rows * probs_stride]: final softmax over survivors */
   uint8_t* masks;                 /* out [num_rows * probs_stride]: bit0 candidate, bit1 top-k, bit2 top-p */
   int64_t probs_stride;
+  const int64_t* history_ends;    /* [num_rows] or NULL (see above) */
 } q3s_batch;
 
 /* Codebook embedding sum after sampling (talker.rs:568-580): for each row,
@@ -245,6 +249,45 @@ int q3s_greedy_batch(q3s_context* ctx, const void* logits, int32_t dtype, int64_
                      int64_t row_stride, int32_t vocab, int64_t suppress_from,
                      int64_t allow_token, int32_t mode, uint32_t* tokens, uint8_t* status,
                      void* stream);
+
+/* ---- device-resident decode frame ---------------------------------------
+ * The host work that follows every Sampler call of the talker and
+ * code-predictor loops, done on the device: the sampled id becomes the next
+ * step's input (Tensor::new(&[next_val]) at code_predictor.rs:365, 414 and
+ * talker.rs:530; the codes of a frame, code_predictor.rs:421), the counter
+ * advances on a draw (sampling.rs:330-332) and the c0 id joins the talker's
+ * history (talker.rs:562-566).  With it, the 16 sampling launches of a frame
+ * (1 talker + 15 code-predictor groups) run back to back with no host round
+ * trip; the caller reads frame_status (and the codes) once per frame.
+ *
+ * For each row r of a finished batched launch, in stream order after it:
+ *   codes[r * codes_stride + group] = tokens[r]            (codes non-NULL)
+ *   if frame_status is NULL or frame_status[r] is OK:
+ *     subseqs[r] += 1 when status[r] is OK and the row sampled (do_sample)
+ *     with history: on OK, history[history_ends[r]++] = tokens[r] if
+ *       history_ends[r] < history_limits[r], else status Q3S_STATUS_HISTORY_FULL
+ *     frame_status[r] = that status                       (frame_status non-NULL)
+ * so a stream's counter and history stop at its first failed call, where the
+ * reference's frame stops with an error.  All pointers are device pointers;
+ * NULL skips that part. */
+typedef struct q3s_commit {
+  int64_t num_rows;
+  const q3s_row_params* params; /* the launch's params (for do_sample) */
+  int64_t params_stride;        /* 0 or 1 */
+  const uint32_t* tokens;       /* the launch's outputs */
+  const uint8_t* status;
+  uint64_t* subseqs;            /* in/out, usually the launch's own subseqs array */
+  uint32_t* codes;              /* [num_rows, codes_stride] frame codes (u32, q3s_embed_sum's input) */
+  int64_t codes_stride;
+  int32_t group;                /* column of this launch's ids */
+  int32_t reserved;
+  uint8_t* frame_status;        /* in/out: first non-OK status of the frame, per row */
+  uint16_t* history;            /* append target (the c0 history of each row) */
+  int64_t* history_ends;        /* in/out: one past each row's last id */
+  const int64_t* history_limits;/* capacity end of each row's history range */
+} q3s_commit;
+
+int q3s_commit_rows(q3s_context* ctx, const q3s_commit* commit, void* stream);
 
 /* ---- stateful sampler: the drop-in for `Sampler` ------------------------ */
 /* Mirrors Sampler (sampling.rs:144-335): one Philox stream (seed, subsequence

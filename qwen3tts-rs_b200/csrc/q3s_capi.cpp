@@ -129,6 +129,8 @@ const char* q3s_status_message(int status) {
       return "vocabulary larger than the sampler supports";
     case Q3S_STATUS_INVALID_CODE:
       return "embedding code outside its codebook";
+    case Q3S_STATUS_HISTORY_FULL:
+      return "c0 history capacity exhausted";
     default:
       return "row not processed";
   }
@@ -213,6 +215,8 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* b, void* stream) {
   a.subseqs = reinterpret_cast<const unsigned long long*>(b->subseqs);
   a.history = b->history;
   a.history_offsets = reinterpret_cast<const long long*>(b->history_offsets);
+  a.history_ends = b->history_offsets ? reinterpret_cast<const long long*>(b->history_ends)
+                                      : nullptr;
   a.tokens = b->tokens;
   a.status = b->status;
   a.uniform_override = b->uniform_override;

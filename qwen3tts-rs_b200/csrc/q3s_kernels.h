@@ -25,6 +25,7 @@ struct KernelArgs {
   const unsigned long long* subseqs;
   const unsigned short* history;
   const long long* history_offsets;
+  const long long* history_ends;  // NULL: row r ends at history_offsets[r + 1]
   unsigned* tokens;
   unsigned char* status;
   const float* uniform_override;

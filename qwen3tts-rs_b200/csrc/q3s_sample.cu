@@ -322,6 +322,11 @@ __device__ __forceinline__ uint32_t clamp16(long long v, int n) {
   return (uint32_t)(uint16_t)(int16_t)c;
 }
 
+// One past the last history id of `row`.
+__device__ __forceinline__ long long history_end(const KernelArgs& a, long long row) {
+  return a.history_ends ? a.history_ends[row] : a.history_offsets[row + 1];
+}
+
 __device__ RowPlan compute_plan(const KernelArgs& a, long long row, uint32_t ticket) {
   const q3s_row_params P = a.params[row * a.params_stride];
   int n = row_vocab(a, row);
@@ -331,7 +336,7 @@ __device__ RowPlan compute_plan(const KernelArgs& a, long long row, uint32_t tic
   if (P.do_sample) flags |= PF_DO_SAMPLE;
   if (P.top_p < 1.0) flags |= PF_TOP_P;
   if (P.do_sample && P.repetition_penalty != 1.0 && a.history_offsets &&
-      a.history_offsets[row + 1] > a.history_offsets[row])
+      history_end(a, row) > a.history_offsets[row])
     flags |= PF_USE_PEN;
   RowPlan p;
   p.u = a.uniform_override ? a.uniform_override[row]
@@ -2358,7 +2363,7 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
     // History bitmap of a sampled row with a penalty (filled while the
     // stage copy may still be in flight).
     if (st == Q3S_STATUS_OK && (pflags & PF_USE_PEN)) {
-      const long long h0 = a.history_offsets[row], h1 = a.history_offsets[row + 1];
+      const long long h0 = a.history_offsets[row], h1 = history_end(a, row);
       fill_history(a.history + h0, h1 - h0, n, f.bm, reinterpret_cast<unsigned char*>(f.list));
     }
     const bool ready = wait_stage(ctl, slot, gen, a.wait_ns);

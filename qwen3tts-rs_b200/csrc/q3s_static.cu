@@ -102,6 +102,8 @@ extern "C" int q3s_sample_batch_static(q3s_context* ctx, const q3s_batch* b, voi
   a.subseqs = reinterpret_cast<const unsigned long long*>(b->subseqs);
   a.history = b->history;
   a.history_offsets = reinterpret_cast<const long long*>(b->history_offsets);
+  a.history_ends = b->history_offsets ? reinterpret_cast<const long long*>(b->history_ends)
+                                      : nullptr;
   a.tokens = b->tokens;
   a.status = b->status;
   a.uniform_override = b->uniform_override;

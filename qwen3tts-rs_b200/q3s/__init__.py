@@ -43,6 +43,7 @@ STATUS_NO_CANDIDATE = 5
 STATUS_INVALID_DENOMINATOR = 6
 STATUS_UNSUPPORTED = 7
 STATUS_INVALID_CODE = 8
+STATUS_HISTORY_FULL = 9
 MAX_CODE_GROUPS = 32
 MAX_VOCAB = 4096
 
@@ -90,6 +91,19 @@ class _Batch(ctypes.Structure):
         ("tokens", ctypes.c_void_p), ("status", ctypes.c_void_p),
         ("uniform_override", ctypes.c_void_p), ("probs", ctypes.c_void_p),
         ("masks", ctypes.c_void_p), ("probs_stride", ctypes.c_int64),
+        ("history_ends", ctypes.c_void_p),
+    ]
+
+
+class _Commit(ctypes.Structure):
+    _fields_ = [
+        ("num_rows", ctypes.c_int64), ("params", ctypes.c_void_p),
+        ("params_stride", ctypes.c_int64), ("tokens", ctypes.c_void_p),
+        ("status", ctypes.c_void_p), ("subseqs", ctypes.c_void_p), ("codes", ctypes.c_void_p),
+        ("codes_stride", ctypes.c_int64), ("group", ctypes.c_int32),
+        ("reserved", ctypes.c_int32), ("frame_status", ctypes.c_void_p),
+        ("history", ctypes.c_void_p), ("history_ends", ctypes.c_void_p),
+        ("history_limits", ctypes.c_void_p),
     ]
 
 
@@ -120,6 +134,7 @@ EXPORTED_SYMBOLS = (
     "q3s_sampler_set_subsequence_counter", "q3s_sampler_get_diagnostics",
     "q3s_sampler_sample_with_mode", "q3s_sampler_sample", "q3s_sample_batch_static",
     "q3s_embed_sum", "q3s_context_set_test_hooks", "q3s_context_set_path_stats",
+    "q3s_commit_rows",
 )
 
 # Row paths of the sampling kernel (Q3S_PATH_* of include/q3s_sampler.h).
@@ -160,6 +175,7 @@ def load(path: Optional[os.PathLike] = None):
     L.q3s_sample_batch_static.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Batch),
                                           ctypes.c_void_p]
     L.q3s_embed_sum.argtypes = [ctypes.c_void_p, ctypes.POINTER(_EmbedBatch), ctypes.c_void_p]
+    L.q3s_commit_rows.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Commit), ctypes.c_void_p]
     L.q3s_greedy_batch.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
@@ -299,7 +315,7 @@ def _dptr(t) -> Optional[int]:
 def sample_batch(logits, params, seeds=None, subseqs=None, *, row_offsets=None, row_vocab=None,
                  vocab: Optional[int] = None, history=None, history_offsets=None,
                  uniform_override=None, debug: bool = False, ctx: Optional[Context] = None,
-                 stream=None, out=None):
+                 stream=None, out=None, history_ends=None):
     """One fused sampling launch over many rows (q3s_sample_batch).
 
     logits: CUDA tensor, float32 or bfloat16, either [R, V] (row stride taken
@@ -315,13 +331,14 @@ def sample_batch(logits, params, seeds=None, subseqs=None, *, row_offsets=None, 
                          row_offsets=row_offsets, row_vocab=row_vocab, vocab=vocab,
                          history=history, history_offsets=history_offsets,
                          uniform_override=uniform_override, debug=debug, ctx=ctx, stream=stream,
-                         out=out)
+                         out=out, history_ends=history_ends)
 
 
 def sample_batch_static(logits, params, seeds=None, subseqs=None, *, row_offsets=None,
                         row_vocab=None, vocab: Optional[int] = None, history=None,
                         history_offsets=None, uniform_override=None, debug: bool = False,
-                        ctx: Optional[Context] = None, stream=None, out=None):
+                        ctx: Optional[Context] = None, stream=None, out=None,
+                        history_ends=None):
     """sample_batch through q3s_sample_batch_static: the same launch with the
     library's file-scope device workspace, so the call itself allocates
     nothing on the device (pass `out` to keep torch from allocating the
@@ -330,7 +347,7 @@ def sample_batch_static(logits, params, seeds=None, subseqs=None, *, row_offsets
                          row_offsets=row_offsets, row_vocab=row_vocab, vocab=vocab,
                          history=history, history_offsets=history_offsets,
                          uniform_override=uniform_override, debug=debug, ctx=ctx, stream=stream,
-                         out=out)
+                         out=out, history_ends=history_ends)
 
 
 class PreparedBatch:
@@ -357,24 +374,26 @@ class PreparedBatch:
 def prepare_batch(logits, params, seeds=None, subseqs=None, *, row_offsets=None,
                   row_vocab=None, vocab: Optional[int] = None, history=None,
                   history_offsets=None, ctx: Optional[Context] = None, out=None,
-                  static: bool = False) -> PreparedBatch:
+                  static: bool = False, history_ends=None) -> PreparedBatch:
     """sample_batch's arguments fixed once; call the result with a stream
     handle to launch (q3s_sample_batch, or q3s_sample_batch_static)."""
     entry = "q3s_sample_batch_static" if static else "q3s_sample_batch"
     b, ctx, keep, tokens, status = _build_batch(
         logits, params, seeds, subseqs, row_offsets=row_offsets, row_vocab=row_vocab,
         vocab=vocab, history=history, history_offsets=history_offsets, uniform_override=None,
-        debug=False, ctx=ctx, out=out)
+        debug=False, ctx=ctx, out=out, history_ends=history_ends)
     return PreparedBatch(entry, b, ctx, keep, tokens, status)
 
 
 def _launch_batch(entry: str, logits, params, seeds, subseqs, *, row_offsets, row_vocab, vocab,
-                  history, history_offsets, uniform_override, debug, ctx, stream, out):
+                  history, history_offsets, uniform_override, debug, ctx, stream, out,
+                  history_ends=None):
     import torch
     b, ctx, keep, tokens, status = _build_batch(
         logits, params, seeds, subseqs, row_offsets=row_offsets, row_vocab=row_vocab,
         vocab=vocab, history=history, history_offsets=history_offsets,
-        uniform_override=uniform_override, debug=debug, ctx=ctx, out=out)
+        uniform_override=uniform_override, debug=debug, ctx=ctx, out=out,
+        history_ends=history_ends)
     dev = logits.device
     s = torch.cuda.current_stream(dev).cuda_stream if stream is None else stream
     _check(getattr(load(), entry)(ctx.handle, ctypes.byref(b), ctypes.c_void_p(s)), entry)
@@ -384,7 +403,7 @@ def _launch_batch(entry: str, logits, params, seeds, subseqs, *, row_offsets, ro
 
 
 def _build_batch(logits, params, seeds, subseqs, *, row_offsets, row_vocab, vocab, history,
-                 history_offsets, uniform_override, debug, ctx, out):
+                 history_offsets, uniform_override, debug, ctx, out, history_ends=None):
     import torch
     dev = logits.device
     if logits.dtype == torch.float32:
@@ -441,8 +460,9 @@ def _build_batch(logits, params, seeds, subseqs, *, row_offsets, row_vocab, voca
     b.probs = _dptr(probs)
     b.masks = _dptr(masks)
     b.probs_stride = V if debug else 0
+    b.history_ends = _dptr(history_ends)
     keep = (logits, params, seeds, subseqs, row_offsets, row_vocab, history, history_offsets,
-            uniform_override, probs, masks)
+            history_ends, uniform_override, probs, masks)
     return b, ctx, keep, tokens, status
 
 
@@ -656,3 +676,36 @@ def path_report(stats) -> dict:
     P = len(PATH_NAMES)
     return {name: {"rows": v[i], "cycles_per_row": v[P + i] / v[i]}
             for i, name in enumerate(PATH_NAMES) if v[i]}
+
+
+def commit_rows(tokens, status, *, params=None, subseqs=None, codes=None, group: int = 0,
+                frame_status=None, history=None, history_ends=None, history_limits=None,
+                ctx: Optional[Context] = None, stream=None) -> None:
+    """The device-side commit after a batched launch (q3s_commit_rows): the
+    ids into column `group` of `codes` ([R, G] int32), the subsequence
+    counters advanced on a draw, the first failure kept in `frame_status`
+    (uint8 [R]) and, with `history`, the ids appended to each row's history
+    range.  Every tensor is on the launch's device; nothing is copied."""
+    import torch
+    R = tokens.numel()
+    c = _Commit()
+    c.num_rows = R
+    if params is not None and isinstance(params, np.ndarray):
+        params = torch.from_numpy(params.view(np.uint8).copy()).to(tokens.device)
+    c.params = _dptr(params)
+    c.params_stride = 0 if params is None or params.numel() // ROW_PARAMS_DTYPE.itemsize == 1 \
+        else 1
+    c.tokens = tokens.data_ptr()
+    c.status = status.data_ptr()
+    c.subseqs = _dptr(subseqs)
+    c.codes = _dptr(codes)
+    c.codes_stride = codes.stride(0) if codes is not None else 0
+    c.group = int(group)
+    c.frame_status = _dptr(frame_status)
+    c.history = _dptr(history)
+    c.history_ends = _dptr(history_ends)
+    c.history_limits = _dptr(history_limits)
+    ctx = ctx or default_context(tokens.device.index)
+    s = torch.cuda.current_stream(tokens.device).cuda_stream if stream is None else stream
+    _check(load().q3s_commit_rows(ctx.handle, ctypes.byref(c), ctypes.c_void_p(s)),
+           "q3s_commit_rows")

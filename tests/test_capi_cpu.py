@@ -38,7 +38,7 @@ def test_library_loads_and_exports_every_declared_symbol():
 
 def test_abi_version_and_status_messages():
     lib = q3s.load()
-    assert lib.q3s_abi_version() == 1
+    assert lib.q3s_abi_version() == 2
     # The reference's error strings (src/talker/sampling.rs:281-296, 642-650,
     # 675-678, 705-718, 58-59).
     expect = {
@@ -51,6 +51,7 @@ def test_abi_version_and_status_messages():
         q3s.STATUS_NO_CANDIDATE: "no finite sampling candidate",
         q3s.STATUS_INVALID_DENOMINATOR: "invalid softmax denominator",
         q3s.STATUS_INVALID_CODE: "embedding code outside its codebook",
+        q3s.STATUS_HISTORY_FULL: "c0 history capacity exhausted",
     }
     for st, msg in expect.items():
         assert q3s.status_message(st) == msg
@@ -66,13 +67,14 @@ def test_struct_layouts_match_binding(tmp_path):
 #include <stdio.h>
 #include "q3s_sampler.h"
 int main(void) {
-  printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\n", sizeof(q3s_row_params),
+  printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\n", sizeof(q3s_row_params),
          offsetof(q3s_row_params, top_k), offsetof(q3s_row_params, do_sample),
          offsetof(q3s_row_params, suppress_from), offsetof(q3s_row_params, allow_token),
          offsetof(q3s_row_params, ctr_lo), sizeof(q3s_batch), offsetof(q3s_batch, probs_stride),
          sizeof(q3s_sampling_options), sizeof(q3s_sampler_diagnostics),
          sizeof(q3s_embed_batch), offsetof(q3s_embed_batch, text_stride),
-         offsetof(q3s_embed_batch, status));
+         offsetof(q3s_embed_batch, status), offsetof(q3s_batch, history_ends),
+         sizeof(q3s_commit), offsetof(q3s_commit, group), offsetof(q3s_commit, history_limits));
   return 0;
 }
 ''')
@@ -87,7 +89,9 @@ int main(void) {
                    dt.fields["ctr_lo"][1], ctypes.sizeof(q3s._Batch),
                    q3s._Batch.probs_stride.offset, ctypes.sizeof(q3s._Options),
                    ctypes.sizeof(q3s._Diagnostics), ctypes.sizeof(q3s._EmbedBatch),
-                   q3s._EmbedBatch.text_stride.offset, q3s._EmbedBatch.status.offset]
+                   q3s._EmbedBatch.text_stride.offset, q3s._EmbedBatch.status.offset,
+                   q3s._Batch.history_ends.offset, ctypes.sizeof(q3s._Commit),
+                   q3s._Commit.group.offset, q3s._Commit.history_limits.offset]
 
 
 def test_context_without_device_fails_cleanly():
