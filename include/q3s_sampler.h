@@ -289,6 +289,74 @@ typedef struct q3s_commit {
 
 int q3s_commit_rows(q3s_context* ctx, const q3s_commit* commit, void* stream);
 
+/* ---- continuous batching of sessions ------------------------------------
+ * The scheduler the reference plans for many concurrent synthesis sessions
+ * (tasks/P12-c-abi-and-continuous-batching.md:11-16: P12-T03 per-session
+ * scheduler state, P12-T04 bounded talker / predictor batching; the
+ * SessionScheduler contract add / tick / cancel of
+ * templates/rust-contracts/session.rs), for the sampling side of a frame.
+ * Each session keeps what its own Sampler and talker loop keep in the
+ * reference: seed and subsequence counter (sampling.rs:144-179), talker and
+ * code-predictor options, the talker suppression, and its c0 history
+ * (talker.rs:500-566), all on the device.  One frame (the contract's tick)
+ * is begin_frame, one step per code group (group 0: the talker row of every
+ * active session, with its history; groups 1..G-1: code-predictor rows),
+ * then end_frame; each step is one sampling launch over all active
+ * sessions plus the device-side commit (q3s_commit_rows), so a session's
+ * ids, counter and history are those it would get alone.
+ *
+ * Sessions join (add) and leave (cancel) between frames: both take effect
+ * at the next begin_frame, which also retires every session whose frame
+ * ended with a non-OK status (the reference's session step returns its
+ * error).  begin_frame reports the active sessions in row order: row r of
+ * every step's logits belongs to ids[r].  All calls of one scheduler go on
+ * one stream, from one host thread. */
+typedef struct q3s_scheduler q3s_scheduler;
+
+typedef struct q3s_session_config {
+  uint64_t id;                    /* unique among the scheduler's sessions */
+  uint64_t seed;                  /* Sampler::new(seed), sampling.rs:158-170 */
+  uint64_t subseq;                /* starting subsequence counter (0 for a new request) */
+  q3s_sampling_options talker;    /* talker options (plan-resolved, talker.rs:452-461) */
+  q3s_sampling_options predictor; /* code-predictor options (code_predictor.rs:357-364) */
+  int32_t talker_do_sample;
+  int32_t predictor_do_sample;
+  int32_t suppress_from;          /* talker row suppression (Q3S_NONE: none) */
+  int32_t allow_token;            /* the token it still allows (EOS), or Q3S_NONE */
+  const uint16_t* history;        /* HOST: initial c0 history, copied by q3s_scheduler_add */
+  int64_t history_len;
+} q3s_session_config;
+
+/* max_sessions slots; `groups` code groups per frame (16 for the 12 Hz
+ * models: 1 talker + 15 code-predictor); history_capacity c0 ids per session
+ * (a session whose history is full stops with Q3S_STATUS_HISTORY_FULL). */
+int q3s_scheduler_create(q3s_context* ctx, int32_t max_sessions, int32_t groups,
+                         int64_t history_capacity, q3s_scheduler** out);
+void q3s_scheduler_destroy(q3s_scheduler* sched);
+/* Joins at the next begin_frame.  Rejects a duplicate id, a history longer
+ * than the capacity, and an add that would exceed max_sessions. */
+int q3s_scheduler_add(q3s_scheduler* sched, const q3s_session_config* config);
+/* Leaves at the next begin_frame (a pending add is simply dropped). */
+int q3s_scheduler_cancel(q3s_scheduler* sched, uint64_t id);
+/* Applies joins and leaves, writes the active session ids in row order to
+ * ids[0 .. min(n, cap)) (HOST) and their number to *n. */
+int q3s_scheduler_begin_frame(q3s_scheduler* sched, uint64_t* ids, int32_t cap, int32_t* n,
+                              void* stream);
+/* Step `group` (0, 1, .. in order): logits row r (device, dtype, `vocab`
+ * entries, row_stride elements apart) belongs to session ids[r]. */
+int q3s_scheduler_step(q3s_scheduler* sched, int32_t group, const void* logits, int32_t dtype,
+                       int32_t vocab, int64_t row_stride, void* stream);
+/* After the last group: one device-to-host copy of the frame's codes
+ * (HOST [n * groups], row-major) and statuses (HOST [n]); synchronises. */
+int q3s_scheduler_end_frame(q3s_scheduler* sched, uint32_t* codes, uint8_t* status,
+                            void* stream);
+/* The frame's codes on the device ([n, groups] u32, the input of
+ * q3s_embed_sum), valid until the next begin_frame. */
+const uint32_t* q3s_scheduler_codes(const q3s_scheduler* sched);
+/* An active session's counter and c0 history (HOST copies; synchronous). */
+int q3s_scheduler_session_state(q3s_scheduler* sched, uint64_t id, uint64_t* subseq,
+                                int64_t* history_len, uint16_t* history, int64_t cap);
+
 /* ---- stateful sampler: the drop-in for `Sampler` ------------------------ */
 /* Mirrors Sampler (sampling.rs:144-335): one Philox stream (seed, subsequence
  * counter) shared by the talker and code-predictor calls of one request. */

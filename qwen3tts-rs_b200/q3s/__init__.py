@@ -95,6 +95,16 @@ class _Batch(ctypes.Structure):
     ]
 
 
+class _SessionConfig(ctypes.Structure):
+    _fields_ = [
+        ("id", ctypes.c_uint64), ("seed", ctypes.c_uint64), ("subseq", ctypes.c_uint64),
+        ("talker", _Options), ("predictor", _Options),
+        ("talker_do_sample", ctypes.c_int32), ("predictor_do_sample", ctypes.c_int32),
+        ("suppress_from", ctypes.c_int32), ("allow_token", ctypes.c_int32),
+        ("history", ctypes.c_void_p), ("history_len", ctypes.c_int64),
+    ]
+
+
 class _Commit(ctypes.Structure):
     _fields_ = [
         ("num_rows", ctypes.c_int64), ("params", ctypes.c_void_p),
@@ -134,7 +144,9 @@ EXPORTED_SYMBOLS = (
     "q3s_sampler_set_subsequence_counter", "q3s_sampler_get_diagnostics",
     "q3s_sampler_sample_with_mode", "q3s_sampler_sample", "q3s_sample_batch_static",
     "q3s_embed_sum", "q3s_context_set_test_hooks", "q3s_context_set_path_stats",
-    "q3s_commit_rows",
+    "q3s_commit_rows", "q3s_scheduler_create", "q3s_scheduler_destroy", "q3s_scheduler_add",
+    "q3s_scheduler_cancel", "q3s_scheduler_begin_frame", "q3s_scheduler_step",
+    "q3s_scheduler_end_frame", "q3s_scheduler_codes", "q3s_scheduler_session_state",
 )
 
 # Row paths of the sampling kernel (Q3S_PATH_* of include/q3s_sampler.h).
@@ -176,6 +188,26 @@ def load(path: Optional[os.PathLike] = None):
                                           ctypes.c_void_p]
     L.q3s_embed_sum.argtypes = [ctypes.c_void_p, ctypes.POINTER(_EmbedBatch), ctypes.c_void_p]
     L.q3s_commit_rows.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Commit), ctypes.c_void_p]
+    L.q3s_scheduler_create.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                       ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p)]
+    L.q3s_scheduler_destroy.argtypes = [ctypes.c_void_p]
+    L.q3s_scheduler_destroy.restype = None
+    L.q3s_scheduler_add.argtypes = [ctypes.c_void_p, ctypes.POINTER(_SessionConfig)]
+    L.q3s_scheduler_cancel.argtypes = [ctypes.c_void_p, ctypes.c_uint64]
+    L.q3s_scheduler_begin_frame.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64),
+                                            ctypes.c_int32, ctypes.POINTER(ctypes.c_int32),
+                                            ctypes.c_void_p]
+    L.q3s_scheduler_step.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
+                                     ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
+                                     ctypes.c_void_p]
+    L.q3s_scheduler_end_frame.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                          ctypes.c_void_p]
+    L.q3s_scheduler_codes.argtypes = [ctypes.c_void_p]
+    L.q3s_scheduler_codes.restype = ctypes.c_void_p
+    L.q3s_scheduler_session_state.argtypes = [ctypes.c_void_p, ctypes.c_uint64,
+                                              ctypes.POINTER(ctypes.c_uint64),
+                                              ctypes.POINTER(ctypes.c_int64), ctypes.c_void_p,
+                                              ctypes.c_int64]
     L.q3s_greedy_batch.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
@@ -709,3 +741,114 @@ def commit_rows(tokens, status, *, params=None, subseqs=None, codes=None, group:
     s = torch.cuda.current_stream(tokens.device).cuda_stream if stream is None else stream
     _check(load().q3s_commit_rows(ctx.handle, ctypes.byref(c), ctypes.c_void_p(s)),
            "q3s_commit_rows")
+
+
+class Scheduler:
+    """Continuous batching of sessions over the sampler (q3s_scheduler_*):
+    each session keeps its own Philox stream, options and c0 history on the
+    device; one frame samples every active session's talker row and code
+    groups, one launch per step.  Joins and leaves take effect at
+    begin_frame, which also retires sessions whose last frame failed."""
+
+    def __init__(self, max_sessions: int, groups: int = 16, history_capacity: int = 4096,
+                 ctx: Optional[Context] = None, device: int = 0):
+        self.ctx = ctx or Context(device)
+        self.groups = int(groups)
+        self.max_sessions = int(max_sessions)
+        self._h = ctypes.c_void_p()
+        _check(load().q3s_scheduler_create(self.ctx.handle, self.max_sessions, self.groups,
+                                           int(history_capacity), ctypes.byref(self._h)),
+               "q3s_scheduler_create")
+        self.active = []
+
+    def add(self, session_id: int, seed: int, talker: SamplingOptions,
+            predictor: SamplingOptions, *, talker_do_sample: bool = True,
+            predictor_do_sample: bool = True, suppress_from=None, allow_token=None,
+            history=(), subseq: int = 0) -> None:
+        h = np.ascontiguousarray(np.asarray(history, dtype=np.uint16))
+        c = _SessionConfig(int(session_id) & (2**64 - 1), int(seed) & (2**64 - 1),
+                           int(subseq) & (2**64 - 1), talker._c(), predictor._c(),
+                           1 if talker_do_sample else 0, 1 if predictor_do_sample else 0,
+                           _none(suppress_from), _none(allow_token),
+                           h.ctypes.data if h.size else None, h.size)
+        _check(load().q3s_scheduler_add(self._h, ctypes.byref(c)), "q3s_scheduler_add")
+
+    def cancel(self, session_id: int) -> None:
+        _check(load().q3s_scheduler_cancel(self._h, int(session_id) & (2**64 - 1)),
+               "q3s_scheduler_cancel")
+
+    def begin_frame(self, stream=None) -> list:
+        import torch
+        ids = (ctypes.c_uint64 * self.max_sessions)()
+        n = ctypes.c_int32(0)
+        s = torch.cuda.current_stream(self.ctx.device).cuda_stream if stream is None else stream
+        _check(load().q3s_scheduler_begin_frame(self._h, ids, self.max_sessions,
+                                                ctypes.byref(n), ctypes.c_void_p(s)),
+               "q3s_scheduler_begin_frame")
+        self.active = list(ids[: n.value])
+        return self.active
+
+    def step(self, group: int, logits, stream=None) -> None:
+        """logits: CUDA tensor [n, V] (float32 or bfloat16), row r for
+        session active[r]."""
+        import torch
+        if logits.dtype == torch.float32:
+            dt = DTYPE_F32
+        elif logits.dtype == torch.bfloat16:
+            dt = DTYPE_BF16
+        else:
+            raise TypeError("logits must be float32 or bfloat16")
+        if logits.dim() != 2 or logits.stride(1) != 1 or logits.shape[0] != len(self.active):
+            raise ValueError("logits must be [active sessions, vocab] with contiguous rows")
+        s = torch.cuda.current_stream(self.ctx.device).cuda_stream if stream is None else stream
+        _check(load().q3s_scheduler_step(self._h, int(group), logits.data_ptr(), dt,
+                                         int(logits.shape[1]), logits.stride(0),
+                                         ctypes.c_void_p(s)), "q3s_scheduler_step")
+
+    def end_frame(self, stream=None):
+        """(codes uint32 [n, groups], status uint8 [n]) of the frame."""
+        import torch
+        n = len(self.active)
+        codes = np.zeros((n, self.groups), np.uint32)
+        status = np.zeros(n, np.uint8)
+        s = torch.cuda.current_stream(self.ctx.device).cuda_stream if stream is None else stream
+        _check(load().q3s_scheduler_end_frame(self._h, codes.ctypes.data, status.ctypes.data,
+                                              ctypes.c_void_p(s)), "q3s_scheduler_end_frame")
+        return codes, status
+
+    def codes_device(self):
+        """The frame's codes as a CUDA int32 tensor [n, groups]: a view of
+        the scheduler's device buffer (no copy), valid until the next
+        begin_frame."""
+        import torch
+        n = len(self.active)
+        ptr = load().q3s_scheduler_codes(self._h)
+
+        class _View:
+            __cuda_array_interface__ = {"shape": (n, self.groups), "typestr": "<i4",
+                                        "data": (int(ptr), False), "version": 3}
+        return torch.as_tensor(_View(), device=f"cuda:{self.ctx.device}")
+
+    def session_state(self, session_id: int):
+        """(subsequence counter, c0 history list) of an active session."""
+        sub = ctypes.c_uint64(0)
+        ln = ctypes.c_int64(0)
+        _check(load().q3s_scheduler_session_state(self._h, int(session_id), ctypes.byref(sub),
+                                                  ctypes.byref(ln), None, 0),
+               "q3s_scheduler_session_state")
+        h = np.zeros(max(ln.value, 1), np.uint16)
+        _check(load().q3s_scheduler_session_state(self._h, int(session_id), ctypes.byref(sub),
+                                                  ctypes.byref(ln), h.ctypes.data, h.size),
+               "q3s_scheduler_session_state")
+        return sub.value, h[: ln.value].tolist()
+
+    def close(self) -> None:
+        if self._h:
+            load().q3s_scheduler_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):  # pragma: no cover - interpreter shutdown order
+        try:
+            self.close()
+        except Exception:
+            pass
