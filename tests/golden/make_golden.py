@@ -1,10 +1,10 @@
 #!/usr/bin/env python3
 """Regenerate the golden vectors under tests/golden/ from the reference.
 
-Run in a container where the reference checkout is mounted read-only at
-/root/reference (it is not needed anywhere else):
+Run where a checkout of the reference (qwen3tts-rs 0.2.0) is available; its
+path is a required argument (nothing else needs the reference):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <path to the checkout>
 
 It reads the reference's own sampling fixtures
 (fixtures/alignment/p02_*.json), transcribes the literal cases of its Rust unit
@@ -280,7 +280,8 @@ def python_oracle_vectors(ref: Path, count: int = 300) -> dict:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--reference", type=Path, required=True,
+                    help="path of the reference checkout (qwen3tts-rs 0.2.0)")
     args = ap.parse_args()
     ref = args.reference
     if not (ref / "src/talker/sampling.rs").exists():
