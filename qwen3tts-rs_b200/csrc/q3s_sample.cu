@@ -2084,80 +2084,131 @@ __device__ __noinline__ unsigned long long nucleus_front(
   return pack_out(Q3S_STATUS_OK, (uint32_t)c);
 }
 
+// The nucleus from nucleus_front's candidates list[0..c) (any order) and the
+// draw.  The stage still holds e = exp(x - Mx) at every element (row[i]),
+// and the row maximum Mx always belongs to the nucleus (it leads the
+// (p desc, index asc) order), so the final softmax terms exp(x - m2) of the
+// reference are the stage's e values: nothing is recomputed.
+//   * topp_walk sorts the candidates' p = e * inv_total as 32-bit keys, one
+//     lane chains the cumulative and a parallel search finds the nucleus size
+//     J; the candidates decide the nucleus when the walk closed and its last
+//     p is above pout, the largest p of an entry outside them, or when no
+//     entry outside them is within 16 of the maximum (else WIDE_GENERAL);
+//   * members (key below the last member's key kJ, and the J - gt entries of
+//     key kJ with the smallest indices) are marked in a bitmap over the
+//     vocabulary, so that one ordered pass over its words lists the nucleus in
+//     vocabulary order with its e values: one lane's sequential f32 prefix
+//     sums and a parallel search for the first running sum >= u * sum.
+// More than 32 candidates tied at the cut (equal p) also return
+// WIDE_GENERAL.  hist: hist[1..3] from nucleus_front, hist[64..192) the
+// member bitmap (n <= 4096); Kb: the e values and prefix sums (512 floats);
+// list[256..512): tied indices, then the nucleus indices (u16).
 __device__ __noinline__ unsigned long long nucleus_finish(uint2* list, unsigned long long* Kb,
-                                                          uint32_t* hist, int c, int n,
-                                                          float top_p, float u,
+                                                          uint32_t* hist, const float* row, int c,
+                                                          int n, float top_p, float u,
                                                           unsigned char* masks, float* probs) {
   const int lane = (int)lane_id();
+  const uint32_t lt = lanemask_lt();
   const float Mx = __uint_as_float(hist[1]);
   const float xout = __uint_as_float(hist[2]);
   const float total = __uint_as_float(hist[3]);
   if (!is_finite(total) || total <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
   const float inv_total = __fdiv_rn(1.0f, total);
-  // (p desc, index asc) over the candidates (sampling.rs:680-689); low bits:
-  // index, then list position.
-  unsigned long long v[8];
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const int j = lane * 8 + r;
-    v[r] = ~0ull;
-    if (j < c) {
-      const uint2 en = list[j];
-      const float p = __fmul_rn(cr_expf_nonpos(__fsub_rn(ex(en), Mx)), inv_total);
-      v[r] = ((unsigned long long)(~__float_as_uint(p)) << 32) | (en.y << 16) | (uint32_t)j;
-    }
-  }
-  bitonic<8>(v);
-#pragma unroll
-  for (int r = 0; r < 8; ++r) Kb[lane * 8 + r] = v[r];
+  float* Bb = reinterpret_cast<float*>(Kb);
+  for (int j = lane; j < c; j += 32) Bb[j] = row[list[j].y];
   __syncwarp();
-  // The walk (sampling.rs:690-697) over the sorted candidates.
-  int J = 0;
-  bool closed = false;
-  float plast = 0.0f;
-  if (lane == 0) {
-    float cum = 0.0f;
-    for (int q = 0; q < 256; ++q) {
-      const unsigned long long key = Kb[q];
-      if (key == ~0ull) break;
-      if (q > 0 && cum >= top_p) {
-        closed = true;
-        break;
-      }
-      const float p = __uint_as_float(~(uint32_t)(key >> 32));
-      cum = __fadd_rn(cum, p);
-      plast = p;
-      J = q + 1;
-    }
-    if (!closed && cum >= top_p) closed = true;  // the next entry, if any, is masked
-  }
-  J = __shfl_sync(FULL, J, 0);
-  closed = __shfl_sync(FULL, closed ? 1 : 0, 0) != 0;
-  plast = __shfl_sync(FULL, plast, 0);
+  uint32_t kJ;
+  int gt;
+  const int J = topp_walk<8>(list, Bb, c, neg_inf(), inv_total, top_p, Bb + 256, kJ, gt);
+  const bool closed = J < c || Bb[256 + c - 1] >= top_p;
   if (xout > neg_inf()) {  // an entry outside the candidates is within 16 of the maximum
     const float pout = __fmul_rn(cr_expf_nonpos(__fsub_rn(xout, Mx)), inv_total);
-    if (!closed || !(plast > pout)) return pack_out(WIDE_GENERAL, 0u);
+    if (!closed || !(__uint_as_float(~kJ) > pout)) return pack_out(WIDE_GENERAL, 0u);
   }
-  // The nucleus, positions [0, J), back into vocabulary order: its keys'
-  // low 32 bits are (index << 16 | list position).
-  uint32_t w[8];
+  // Members into the bitmap; candidates tied at the cut listed aside.
+  const int need = J - gt;
+  uint32_t* bm = hist + 64;
+  const int W = (n + 31) >> 5;
+  for (int w = lane; w < W; w += 32) bm[w] = 0u;
+  __syncwarp();
+  uint16_t* tie = reinterpret_cast<uint16_t*>(list + 256);
+  int T = 0;
+  for (int j0 = 0; j0 < c; j0 += 32) {
+    const int j = j0 + lane;
+    uint32_t key = 0xFFFFFFFFu, idx = 0u;
+    if (j < c) {
+      idx = list[j].y;
+      key = ~__float_as_uint(__fmul_rn(Bb[j], inv_total));
+    }
+    if (key < kJ) atomicOr(&bm[idx >> 5], 1u << (idx & 31));
+    const unsigned tb = __ballot_sync(FULL, key == kJ);
+    if (key == kJ && T + __popc(tb & lt) < 32) tie[T + __popc(tb & lt)] = (uint16_t)idx;
+    T += __popc(tb);
+  }
+  __syncwarp();
+  if (T > 32) return pack_out(WIDE_GENERAL, 0u);
+  {
+    const uint32_t mine = lane < T ? tie[lane] : 0xFFFFu;
+    int rank = 0;
+    for (int t = 0; t < T; ++t) rank += __shfl_sync(FULL, mine, t) < mine ? 1 : 0;
+    if (lane < T && rank < need) atomicOr(&bm[mine >> 5], 1u << (mine & 31));
+  }
+  __syncwarp();
+  // The nucleus in vocabulary order: lane l takes words [l * wpl, (l+1) * wpl).
+  const int wpl = (W + 31) >> 5;
+  int cnt = 0;
+  for (int k = 0; k < wpl; ++k) {
+    const int w = lane * wpl + k;
+    if (w < W) cnt += __popc(bm[w]);
+  }
+  const int incl = (int)warp_inclusive_scan((uint32_t)cnt);
+  const int J2 = __shfl_sync(FULL, incl, 31);
+  uint16_t* nidx = reinterpret_cast<uint16_t*>(list + 256);
+  int pos = incl - cnt;
+  for (int k = 0; k < wpl; ++k) {
+    const int w = lane * wpl + k;
+    uint32_t bits = w < W ? bm[w] : 0u;
+    while (bits) {
+      const int i = (w << 5) + __ffs(bits) - 1;
+      bits &= bits - 1;
+      Bb[pos] = row[i];
+      nidx[pos] = (uint16_t)i;
+      ++pos;
+    }
+  }
+  if (lane < ((8 - (J2 & 7)) & 7)) Bb[J2 + lane] = 0.0f;  // zero-pad to a multiple of 8
+  __syncwarp();
+  // Final softmax sum and the draw (sampling.rs:700-729) over e = exp(x - Mx).
+  float* E = Bb;
+  // The debug outputs keep the terms: the chain overwrites them with running
+  // sums.  J2 = J <= 256 members, at most 8 per lane.
+  float ev[8];
 #pragma unroll
-  for (int r = 0; r < 8; ++r) w[r] = lane * 8 + r < J ? (uint32_t)v[r] : 0xFFFFFFFFu;
-  bitonic<8>(w);
-  uint2* nuc = list + 256;  // the nucleus, in vocabulary order
-  float m2 = neg_inf();
+  for (int r = 0; r < 8; ++r) ev[r] = (masks || probs) && lane + 32 * r < J2 ? E[lane + 32 * r] : 0.0f;
+  const float sum = chain_smem<true>(E, J2);
+  if (!is_finite(sum) || sum <= 0.0f) return pack_out(Q3S_STATUS_INVALID_DENOMINATOR, 0u);
+  const float thr = __fmul_rn(u, sum);
+  uint32_t token = (uint32_t)(n - 1);
+  for (int q0 = 0; q0 < J2; q0 += 32) {
+    const int q = q0 + lane;
+    const unsigned bb = __ballot_sync(FULL, q < J2 && E[q] >= thr);
+    if (bb) {
+      token = nidx[q0 + __ffs(bb) - 1];
+      break;
+    }
+  }
+  if (masks || probs) {
 #pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    if (lane * 8 + r < J) {
-      const uint2 en = list[w[r] & 0xFFFFu];
-      nuc[lane * 8 + r] = en;
-      m2 = fmaxf(m2, ex(en));
+    for (int r = 0; r < 8; ++r) {
+      const int q = lane + 32 * r;
+      if (q >= J2) continue;
+      const int i = nidx[q];
+      if (masks) masks[i] |= 4;
+      if (probs) probs[i] = __double2float_rn((double)ev[r] / (double)sum);
     }
   }
   __syncwarp();
-  m2 = warp_max(m2);
-  if (!(m2 > neg_inf())) return pack_out(Q3S_STATUS_NO_CANDIDATE, 0u);
-  return draw_tail(nuc, J, n, m2, u, reinterpret_cast<float*>(Kb), masks, probs);
+  return pack_out(Q3S_STATUS_OK, token);
 }
 
 // A sampled row: fast path when it applies, else the general path.
@@ -2257,11 +2308,11 @@ general:
       unsigned long long r =
           nucleus_front<NJ>(f.stage, f.list, f.hist, f.bm, s.n, s.mis, rc.inv, rc.pf,
                             rc.use_pen ? 1 : 0, rc.sf, rc.allow, exact ? 0 : 1, rc.nj);
-      release<DT>(rel);
       if ((int)(r >> 32) == Q3S_STATUS_OK) {
-        r = nucleus_finish(f.list, f.Kb, f.hist, (int)(uint32_t)r, s.n, pl.top_p, u, dbg.masks,
-                           dbg.probs);
+        r = nucleus_finish(f.list, f.Kb, f.hist, reinterpret_cast<const float*>(f.stage) + s.mis,
+                           (int)(uint32_t)r, s.n, pl.top_p, u, dbg.masks, dbg.probs);
       }
+      release<DT>(rel);
       const RowOut out{(int)(r >> 32), (uint32_t)r};
       path = out.status == WIDE_GENERAL ? Q3S_PATH_GENERAL_NUCLEUS : Q3S_PATH_NUCLEUS;
       if (out.status != WIDE_GENERAL) {
