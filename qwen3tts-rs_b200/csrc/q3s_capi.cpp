@@ -48,8 +48,10 @@ struct SingleRow {
   q3s_row_params params;
   unsigned long long seed;
   unsigned long long subseq;
-  long long hoff[2];
+  long long hist_len;
 };
+
+int launch_batch(q3s_context* ctx, const q3s_batch* b, const SingleRow* row, void* stream);
 
 }  // namespace
 
@@ -58,13 +60,18 @@ struct q3s_context {
   int sm_count = 0;
   size_t smem_optin = 0;
   std::mutex mu;
-  // Single-row staging (stateful sampler calls).
-  SingleRow* h_row = nullptr;  // pinned
-  void* d_row = nullptr;       // device SingleRow
+  // Single-row staging (stateful sampler calls).  The row's parameters go
+  // in the kernel arguments.  d_hist holds the last history uploaded, and
+  // h_hist (pinned) a copy of its first hist_dev ids, so a call whose
+  // history extends that one uploads only the new ids (the talker's c0
+  // history grows by one id per frame).  The token and status byte are
+  // written by the kernel straight into h_out (mapped pinned memory; d_out
+  // is its device address), so no copy is issued for them.
   uint16_t* h_hist = nullptr;  // pinned
   uint16_t* d_hist = nullptr;
   size_t hist_cap = 0;
-  unsigned* h_out = nullptr;  // pinned: token, status byte in the next word
+  size_t hist_dev = 0;
+  unsigned* h_out = nullptr;  // mapped pinned: token, status byte in the next word
   unsigned* d_out = nullptr;
   // General-path workspaces of the sampling kernel, one per stream that has
   // launched through this context (grown on demand), so launches on
@@ -168,12 +175,9 @@ void q3s_context_destroy(q3s_context* c) {
   if (!c) return;
   {
     DeviceGuard g(c->device);
-    if (c->h_row) cudaFreeHost(c->h_row);
-    if (c->d_row) cudaFree(c->d_row);
     if (c->h_hist) cudaFreeHost(c->h_hist);
     if (c->d_hist) cudaFree(c->d_hist);
     if (c->h_out) cudaFreeHost(c->h_out);
-    if (c->d_out) cudaFree(c->d_out);
     for (auto& w : c->ws)
       if (w.ptr) cudaFree(w.ptr);
   }
@@ -199,6 +203,18 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* b, void* stream) {
     return fail(Q3S_E_INVALID_ARGUMENT, "history_offsets without history");
   if ((b->probs || b->masks) && b->probs_stride < b->vocab)
     return fail(Q3S_E_INVALID_ARGUMENT, "probs_stride must be >= vocab");
+  return launch_batch(ctx, b, nullptr, stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+// The launch of a validated batch.  `row` (single-row calls of the stateful
+// sampler): the row's parameters, Philox key and counter and history length
+// travel in the kernel arguments instead of b->params / seeds / subseqs /
+// history_offsets.
+int launch_batch(q3s_context* ctx, const q3s_batch* b, const SingleRow* row, void* stream) {
   DeviceGuard g(ctx->device);
   if (g.err != cudaSuccess) return cuda_fail(g.err, "cudaSetDevice");
   q3s::KernelArgs a;
@@ -226,6 +242,13 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* b, void* stream) {
   if (ctx->test_wait_ns) a.wait_ns = ctx->test_wait_ns;
   a.hold_refill = ctx->test_hold_refill;
   a.path_stats = ctx->path_stats;
+  if (row) {
+    a.inline_row = 1;
+    a.row_params = row->params;
+    a.row_seed = row->seed;
+    a.row_subseq = row->subseq;
+    a.row_hist_len = row->hist_len;
+  }
   int cap = b->vocab < Q3S_MAX_VOCAB ? b->vocab : Q3S_MAX_VOCAB;
   a.vcap = ((cap > 0 ? cap : 1) + 31) / 32 * 32;
   int warps = q3s::sample_max_warps(a.vcap, b->dtype, ctx->smem_optin);
@@ -266,6 +289,10 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* b, void* stream) {
   if (e != cudaSuccess) return cuda_fail(e, "sample kernel launch");
   return Q3S_OK;
 }
+
+}  // namespace
+
+extern "C" {
 
 int q3s_context_set_test_hooks(q3s_context* ctx, uint64_t stage_wait_ns, int32_t hold_refill) {
   if (!ctx) return fail(Q3S_E_INVALID_ARGUMENT, "q3s_context_set_test_hooks: NULL context");
@@ -337,14 +364,14 @@ static uint32_t sat_inc(uint32_t v) { return v == 0xFFFFFFFFu ? v : v + 1; }
 
 static int ensure_single_row(q3s_context* c, int64_t hist_len) {
   cudaError_t e;
-  if (!c->h_row) {
-    if ((e = cudaMallocHost((void**)&c->h_row, sizeof(SingleRow))) != cudaSuccess)
-      return cuda_fail(e, "cudaMallocHost");
-    if ((e = cudaMalloc(&c->d_row, sizeof(SingleRow))) != cudaSuccess)
-      return cuda_fail(e, "cudaMalloc");
-    if ((e = cudaMallocHost((void**)&c->h_out, 16)) != cudaSuccess)
-      return cuda_fail(e, "cudaMallocHost");
-    if ((e = cudaMalloc((void**)&c->d_out, 16)) != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+  if (!c->h_out) {
+    if ((e = cudaHostAlloc((void**)&c->h_out, 16, cudaHostAllocMapped)) != cudaSuccess)
+      return cuda_fail(e, "cudaHostAlloc(mapped)");
+    if ((e = cudaHostGetDevicePointer((void**)&c->d_out, c->h_out, 0)) != cudaSuccess) {
+      cudaFreeHost(c->h_out);
+      c->h_out = nullptr;
+      return cuda_fail(e, "cudaHostGetDevicePointer");
+    }
   }
   if ((size_t)hist_len > c->hist_cap) {
     size_t cap = c->hist_cap ? c->hist_cap : 1024;
@@ -354,6 +381,7 @@ static int ensure_single_row(q3s_context* c, int64_t hist_len) {
     c->h_hist = nullptr;
     c->d_hist = nullptr;
     c->hist_cap = 0;
+    c->hist_dev = 0;
     if ((e = cudaMallocHost((void**)&c->h_hist, cap * sizeof(uint16_t))) != cudaSuccess)
       return cuda_fail(e, "cudaMallocHost");
     if ((e = cudaMalloc((void**)&c->d_hist, cap * sizeof(uint16_t))) != cudaSuccess)
@@ -372,6 +400,8 @@ int q3s_sampler_sample_with_mode(q3s_sampler* s, const void* logits, int32_t dty
   if (!s || !o || !token || (hist_len > 0 && !history) || hist_len < 0 || n < 0)
     return fail(Q3S_E_INVALID_ARGUMENT, "q3s_sampler_sample_with_mode: bad argument");
   if (n > 0 && !logits) return fail(Q3S_E_INVALID_ARGUMENT, "logits is NULL");
+  if (dtype != Q3S_DTYPE_F32 && dtype != Q3S_DTYPE_BF16)
+    return fail(Q3S_E_INVALID_ARGUMENT, "dtype must be Q3S_DTYPE_F32 or Q3S_DTYPE_BF16");
   if (n > Q3S_MAX_VOCAB) {
     if (row_status) *row_status = Q3S_STATUS_UNSUPPORTED;
     return fail(Q3S_E_SAMPLING, q3s_status_message(Q3S_STATUS_UNSUPPORTED));
@@ -409,7 +439,7 @@ int q3s_sampler_sample_with_mode(q3s_sampler* s, const void* logits, int32_t dty
   int rc = ensure_single_row(c, need_hist ? hist_len : 0);
   if (rc != Q3S_OK) return rc;
   cudaStream_t st_ = (cudaStream_t)stream;
-  SingleRow& r = *c->h_row;
+  SingleRow r;
   std::memset(&r, 0, sizeof(r));
   r.params.temperature = o->temperature;
   r.params.top_p = o->top_p;
@@ -424,19 +454,27 @@ int q3s_sampler_sample_with_mode(q3s_sampler* s, const void* logits, int32_t dty
   r.params.ctr_lo = s->ctr_lo;
   r.seed = s->seed;
   r.subseq = s->subseq;
-  r.hoff[0] = 0;
-  r.hoff[1] = need_hist ? hist_len : 0;
+  r.hist_len = need_hist ? hist_len : 0;
   cudaError_t e;
   if (need_hist) {
-    std::memcpy(c->h_hist, history, (size_t)hist_len * sizeof(uint16_t));
-    if ((e = cudaMemcpyAsync(c->d_hist, c->h_hist, (size_t)hist_len * sizeof(uint16_t),
-                             cudaMemcpyHostToDevice, st_)) != cudaSuccess)
-      return cuda_fail(e, "history upload");
+    // Upload only what the device copy lacks: everything after the ids it
+    // already holds, when this history starts with them.
+    const size_t len = (size_t)hist_len;
+    size_t keep = c->hist_dev <= len &&
+                          std::memcmp(c->h_hist, history, c->hist_dev * sizeof(uint16_t)) == 0
+                      ? c->hist_dev
+                      : 0;
+    if (keep < len) {
+      std::memcpy(c->h_hist + keep, history + keep, (len - keep) * sizeof(uint16_t));
+      if ((e = cudaMemcpyAsync(c->d_hist + keep, c->h_hist + keep,
+                               (len - keep) * sizeof(uint16_t), cudaMemcpyHostToDevice, st_)) !=
+          cudaSuccess) {
+        c->hist_dev = 0;
+        return cuda_fail(e, "history upload");
+      }
+    }
+    c->hist_dev = len;
   }
-  if ((e = cudaMemcpyAsync(c->d_row, c->h_row, sizeof(SingleRow), cudaMemcpyHostToDevice, st_)) !=
-      cudaSuccess)
-    return cuda_fail(e, "parameter upload");
-  SingleRow* dr = static_cast<SingleRow*>(c->d_row);
   q3s_batch b;
   std::memset(&b, 0, sizeof(b));
   b.logits = logits ? logits : c->d_out;  // n == 0 reads nothing
@@ -444,24 +482,18 @@ int q3s_sampler_sample_with_mode(q3s_sampler* s, const void* logits, int32_t dty
   b.vocab = (int32_t)n;
   b.num_rows = 1;
   b.row_stride = 0;
-  b.params = &dr->params;
-  b.params_stride = 0;
-  b.seeds = reinterpret_cast<const uint64_t*>(&dr->seed);
-  b.subseqs = reinterpret_cast<const uint64_t*>(&dr->subseq);
   b.history = need_hist ? c->d_hist : nullptr;
-  b.history_offsets = need_hist ? reinterpret_cast<const int64_t*>(dr->hoff) : nullptr;
   b.tokens = c->d_out;
   b.status = reinterpret_cast<uint8_t*>(c->d_out + 1);
-  rc = q3s_sample_batch(c, &b, stream);
+  rc = launch_batch(c, &b, &r, stream);
   if (rc != Q3S_OK) return rc;
-  if ((e = cudaMemcpyAsync(c->h_out, c->d_out, 8, cudaMemcpyDeviceToHost, st_)) != cudaSuccess)
-    return cuda_fail(e, "result download");
   if ((e = cudaStreamSynchronize(st_)) != cudaSuccess) return cuda_fail(e, "stream synchronize");
   if (observer) observer(observer_user_data, 0, Q3S_TRANSFER_SAMPLED_TOKEN, 1);
-  const int rs = (int)(c->h_out[1] & 0xFFu);
+  const volatile unsigned* out = c->h_out;
+  const int rs = (int)(out[1] & 0xFFu);
   if (row_status) *row_status = rs;
   if (rs != Q3S_STATUS_OK) return fail(Q3S_E_SAMPLING, q3s_status_message(rs));
-  *token = c->h_out[0];
+  *token = out[0];
   // The counter moves only for a sampled call that drew (sampling.rs:330-332).
   if (do_sample) s->subseq += 1;
   return Q3S_OK;

@@ -42,6 +42,13 @@ struct KernelArgs {
   // Diagnostics (q3s_context_set_path_stats): per Q3S_PATH_* row counts and
   // warp cycles, accumulated by the debug instantiation; NULL in production.
   unsigned long long* path_stats = nullptr;
+  // A single-row launch (the stateful sampler) passes its row by value:
+  // parameters, Philox key and counter, and the length of its history at
+  // `history` (no history_offsets), so nothing but the history is uploaded.
+  int inline_row = 0;
+  q3s_row_params row_params{};
+  unsigned long long row_seed = 0, row_subseq = 0;
+  long long row_hist_len = 0;
 };
 
 size_t sample_smem_per_warp(int vcap, int dtype);

@@ -322,25 +322,32 @@ __device__ __forceinline__ uint32_t clamp16(long long v, int n) {
   return (uint32_t)(uint16_t)(int16_t)c;
 }
 
-// One past the last history id of `row`.
+// The history range of `row`: [history_begin, history_end).
+__device__ __forceinline__ long long history_begin(const KernelArgs& a, long long row) {
+  return a.inline_row ? 0 : a.history_offsets[row];
+}
+
 __device__ __forceinline__ long long history_end(const KernelArgs& a, long long row) {
+  if (a.inline_row) return a.row_hist_len;
   return a.history_ends ? a.history_ends[row] : a.history_offsets[row + 1];
 }
 
 __device__ RowPlan compute_plan(const KernelArgs& a, long long row, uint32_t ticket) {
-  const q3s_row_params P = a.params[row * a.params_stride];
+  const q3s_row_params P = a.inline_row ? a.row_params : a.params[row * a.params_stride];
   int n = row_vocab(a, row);
   const int st = row_fits(a, n) ? validate(P) : Q3S_STATUS_UNSUPPORTED;
   n = n < 0 ? 0 : (n > 65535 ? 65535 : n);
   uint32_t flags = (uint32_t)st;
   if (P.do_sample) flags |= PF_DO_SAMPLE;
   if (P.top_p < 1.0) flags |= PF_TOP_P;
-  if (P.do_sample && P.repetition_penalty != 1.0 && a.history_offsets &&
-      history_end(a, row) > a.history_offsets[row])
+  if (P.do_sample && P.repetition_penalty != 1.0 && (a.inline_row ? a.history != nullptr
+                                                                  : a.history_offsets != nullptr) &&
+      history_end(a, row) > history_begin(a, row))
     flags |= PF_USE_PEN;
   RowPlan p;
   p.u = a.uniform_override ? a.uniform_override[row]
-                           : philox_uniform(a.seeds[row], a.subseqs[row], P.ctr_lo);
+          : a.inline_row ? philox_uniform(a.row_seed, a.row_subseq, P.ctr_lo)
+                         : philox_uniform(a.seeds[row], a.subseqs[row], P.ctr_lo);
   p.inv = __fdiv_rn(1.0f, (float)P.temperature);
   p.pf = (float)P.repetition_penalty;
   p.top_p = (float)P.top_p;
@@ -2414,7 +2421,7 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
     // History bitmap of a sampled row with a penalty (filled while the
     // stage copy may still be in flight).
     if (st == Q3S_STATUS_OK && (pflags & PF_USE_PEN)) {
-      const long long h0 = a.history_offsets[row], h1 = history_end(a, row);
+      const long long h0 = history_begin(a, row), h1 = history_end(a, row);
       fill_history(a.history + h0, h1 - h0, n, f.bm, reinterpret_cast<unsigned char*>(f.list));
     }
     const bool ready = wait_stage(ctl, slot, gen, a.wait_ns);

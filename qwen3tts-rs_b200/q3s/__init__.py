@@ -668,7 +668,11 @@ class Sampler:
         dt = DTYPE_F32 if x.dtype == torch.float32 else DTYPE_BF16
         if x.dtype not in (torch.float32, torch.bfloat16):
             raise TypeError("logits must be float32 or bfloat16")
-        h = np.ascontiguousarray(np.asarray(history, dtype=np.uint16))
+        if isinstance(history, np.ndarray) and history.dtype == np.uint16 and \
+                history.flags.c_contiguous:
+            h = history
+        else:
+            h = np.ascontiguousarray(np.asarray(history, dtype=np.uint16))
         tok = ctypes.c_uint32(0)
         st = ctypes.c_int32(0)
         cb = TRANSFER_CALLBACK(0)
