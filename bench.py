@@ -45,9 +45,9 @@ HETERO_STREAMS = 4096
 BYTES_PER_ROW = 4 * VOCAB + 16 + 4 + 1
 # DRAM bytes (read + write) per 65,536-row launch of the sampling kernel: an
 # ncu capture of a 16,384-row launch (dram__bytes_read.sum +
-# dram__bytes_write.sum = 210.2 MB) scaled by the rows, since every row is
-# read from HBM exactly once.
-NCU_TRAFFIC_PER_LAUNCH = 210.206208e6 * 4
+# dram__bytes_write.sum = 201.810176 + 6.509312 MB) scaled by the rows, since
+# every row is read from HBM exactly once.
+NCU_TRAFFIC_PER_LAUNCH = 208.319488e6 * 4
 FALLBACK_HBM_GBS = 6650.0
 L2_FLUSH_BYTES = 256 << 20
 
@@ -274,7 +274,11 @@ def main() -> int:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
-    ap.add_argument("--hetero-steps", type=int, default=100)
+    ap.add_argument("--hetero-steps", type=int, default=100,
+                    help="timed launches of the heterogeneous leg (0 skips the leg)")
+    ap.add_argument("--hetero-streams", type=int, default=HETERO_STREAMS,
+                    help="streams of the heterogeneous leg (smaller cases are for profiler "
+                         "captures only)")
     ap.add_argument("--rows", type=int, default=ROWS,
                     help="rows per GPU (smaller cases are for profiler captures only)")
     args = ap.parse_args()
@@ -433,8 +437,10 @@ def main() -> int:
 
     del w, launch
     torch.cuda.empty_cache()
-    hetero = hetero_leg(args, world, rank, dev, ctx, q3s, workloads, shard, np, torch, oracle,
-                        peak, max_over_ranks, gather)
+    hetero = None
+    if args.hetero_steps > 0:
+        hetero = hetero_leg(args, world, rank, dev, ctx, q3s, workloads, shard, np, torch, oracle,
+                            peak, max_over_ranks, gather)
 
     results = {"hetero_decode_step": hetero}
     cpu = None
@@ -491,8 +497,9 @@ def hetero_leg(args, world, rank, dev, ctx, q3s, workloads, shard, np, torch, or
     3072 + 15 code-predictor rows of 2048), whole streams sharded over the
     ranks; L2 flushed between launches.  Every rank checks a row sample of
     its shard against the oracle."""
-    w = workloads.hetero(dev, streams=HETERO_STREAMS)
-    r0, r1 = shard.stream_range(HETERO_STREAMS, 16, world, rank)
+    streams = args.hetero_streams
+    w = workloads.hetero(dev, streams=streams)
+    r0, r1 = shard.stream_range(streams, 16, world, rank)
     a = w.device_args(dev)
     R = r1 - r0
     hoff = a["history_offsets"]
@@ -521,7 +528,7 @@ def hetero_leg(args, world, rank, dev, ctx, q3s, workloads, shard, np, torch, or
     gbs = [p["bytes"] / (p["ms"] / 1e3) / 1e9 for p in per]
     del w, launch, flush
     torch.cuda.empty_cache()
-    return {"streams": HETERO_STREAMS, "rows_total": total_rows, "n_gpus": world,
+    return {"streams": streams, "rows_total": total_rows, "n_gpus": world,
             "rows_per_s": total_rows / (ms_max / 1e3), "ms_per_launch_max": ms_max,
             "gbs_per_gpu": gbs, "hbm_frac_per_gpu": [g / peak for g in gbs],
             "l2": "flushed between launches", "parity_rows_checked_per_rank": int(sel.size),
@@ -622,11 +629,13 @@ def secondary(ctx, dev, q3s, workloads, np, torch):
         raise RuntimeError("embedding sum failed")
     out["embed_sum_4096x16_h2048_bf16"] = res
     del tables, text, eout
-    # Single-stream talker step through the stateful Sampler (host round trip).
-    ws = workloads.talker_single(dev, steps=200)
+    # Single-stream talker step through the stateful Sampler (host round trip),
+    # broken down: the binding call, the bare C call, the kernel alone.
+    import ctypes
+    ws = workloads.talker_single(dev, steps=400)
     s = q3s.Sampler(42, ctx)
     o = q3s.SamplingOptions(0.9, 50, 1.0, 1.05)
-    hist = list(ws.history[:256])
+    hist = np.ascontiguousarray(ws.history[:256])
     for i in range(5):
         s.sample_with_mode(ws.logits[i], o, True, 2048, 2150, hist)
     torch.cuda.synchronize()
@@ -634,16 +643,49 @@ def secondary(ctx, dev, q3s, workloads, np, torch):
     for i in range(200):
         s.sample_with_mode(ws.logits[i], o, True, 2048, 2150, hist)
     dt = time.perf_counter() - t0
+    grow = list(hist)
+    t0 = time.perf_counter()
+    for i in range(200):
+        tok = s.sample_with_mode(ws.logits[200 + i], o, True, 2048, 2150,
+                                 np.array(grow, np.uint16))
+        grow.append(tok % 2048)
+    dt_grow = time.perf_counter() - t0
+    L = q3s.load()
+    copt = o._c()
+    tok_c, st_c = ctypes.c_uint32(0), ctypes.c_int32(0)
+    cb = q3s.TRANSFER_CALLBACK(0)
+    hp = hist.ctypes.data_as(ctypes.c_void_p)
+    ptrs = [ctypes.c_void_p(ws.logits[i].data_ptr()) for i in range(200)]
+    stream_c = ctypes.c_void_p(sh)
+    t0 = time.perf_counter()
+    for i in range(200):
+        L.q3s_sampler_sample_with_mode(s._h, ptrs[i], q3s.DTYPE_F32, 3072, ctypes.byref(copt), 1,
+                                       2048, 2150, hp, 256, cb, None, ctypes.byref(tok_c),
+                                       ctypes.byref(st_c), stream_c)
+    dt_c = time.perf_counter() - t0
     aw = ws.device_args(dev)
     one = q3s.prepare_batch(ws.logits[0:1], aw["params"], aw["seeds"][:1], aw["subseqs"][:1],
                             history=aw["history"], history_offsets=aw["history_offsets"][:2],
                             ctx=ctx)
     kms = time_each(torch, lambda: one(sh), 50, flush)
-    out["talker_single_step"] = {"us_per_step": dt * 1e6 / 200,
-                                 "kernel_us": kms * 1e3,
-                                 "note": "stateful Sampler call incl. H2D params/history and "
-                                         "D2H token+status, host wall clock; kernel_us is the "
-                                         "1-row launch alone (CUDA events, L2 flushed)"}
+    kms_warm = time_each(torch, lambda: one(sh), 50)
+    t0 = time.perf_counter()
+    for _ in range(200):
+        one(sh)
+    enq = (time.perf_counter() - t0) / 200
+    torch.cuda.synchronize()
+    out["talker_single_step"] = {
+        "us_per_step": dt * 1e6 / 200,
+        "us_per_step_growing_history": dt_grow * 1e6 / 200,
+        "c_call_us": dt_c * 1e6 / 200,
+        "kernel_us_l2_warm": kms_warm * 1e3,
+        "kernel_us_l2_flushed": kms * 1e3,
+        "launch_enqueue_us": enq * 1e6,
+        "note": "us_per_step: stateful Sampler call through the Python binding (256-id "
+                "history, host wall clock, includes the sync and the token read); "
+                "growing: the history grows by one id per step as the talker's does; "
+                "c_call_us: the same C entry point called with prebuilt arguments; "
+                "kernel_us: the 1-row launch alone (CUDA events)"}
     return out
 
 
