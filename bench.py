@@ -629,6 +629,39 @@ def secondary(ctx, dev, q3s, workloads, np, torch):
         raise RuntimeError("embedding sum failed")
     out["embed_sum_4096x16_h2048_bf16"] = res
     del tables, text, eout
+    # Producer fusion: the talker's codec_head projection (3072 x 1024 bf16)
+    # and the sampling of its rows in one launch, against the matmul followed
+    # by the sampling launch; L2 flushed before each (the weights are not
+    # assumed resident).
+    hg = torch.Generator(device=dev).manual_seed(21)
+    weight = (torch.randn((3072, 1024), generator=hg, device=dev) * 0.05).to(torch.bfloat16)
+    head = {}
+    for R in (1, 16):
+        hidden = torch.randn((R, 1024), generator=hg, device=dev).to(torch.bfloat16)
+        hp = q3s.make_params(R, temperature=0.9, top_k=50, top_p=1.0, repetition_penalty=1.0,
+                             suppress_from=2048, allow_token=2150)
+        dp = torch.from_numpy(hp.view(np.uint8).copy()).to(dev)
+        ds = torch.arange(R, dtype=torch.int64, device=dev)
+        du = torch.zeros(R, dtype=torch.int64, device=dev)
+        hout = (torch.empty(R, dtype=torch.int32, device=dev),
+                torch.empty(R, dtype=torch.uint8, device=dev),
+                torch.empty((R, 3072), dtype=torch.float32, device=dev))
+        fused = time_each(torch, lambda: q3s.head_sample(hidden, weight, dp, ds, du, ctx=ctx,
+                                                         out=hout), 50, flush)
+        lg = torch.empty((R, 3072), dtype=torch.bfloat16, device=dev)
+        sout = (torch.empty(R, dtype=torch.int32, device=dev),
+                torch.empty(R, dtype=torch.uint8, device=dev))
+
+        def unfused():
+            torch.matmul(hidden, weight.t(), out=lg)  # bf16 logits, as the model's linear
+            q3s.sample_batch(lg, dp, ds, du, ctx=ctx, out=sout)
+        sep = time_each(torch, unfused, 50, flush)
+        head[f"rows_{R}"] = {"fused_us": fused * 1e3, "matmul_then_sample_us": sep * 1e3}
+    out["head_sample_3072x1024_bf16"] = dict(head, note="q3s_head_sample (projection and "
+                                             "sampling in one launch) against torch.matmul "
+                                             "(bf16 logits) followed by q3s_sample_batch; "
+                                             "CUDA events, L2 flushed before each launch")
+    del weight
     # Single-stream talker step through the stateful Sampler (host round trip),
     # broken down: the binding call, the bare C call, the kernel alone.
     import ctypes

@@ -250,6 +250,39 @@ int q3s_greedy_batch(q3s_context* ctx, const void* logits, int32_t dtype, int64_
                      int64_t allow_token, int32_t mode, uint32_t* tokens, uint8_t* status,
                      void* stream);
 
+/* ---- producer fusion: head projection + sampling --------------------------
+ * The logits of a decode step come from a head projection without bias,
+ * logits = hidden · weightᵀ: the talker's codec_head (talker.rs:87-89, used
+ * at :501) and the code predictor's lm_heads[g] (code_predictor.rs:402),
+ * via primitives.rs:32-42.  q3s_head_sample computes that projection and
+ * samples its rows in one launch, for the small batches of the decode loop
+ * (at most Q3S_HEAD_MAX_ROWS rows): every block computes a slice of the
+ * logits (f32 products and sums of the bf16 weights and the hidden values,
+ * in a fixed order, so every launch gives the same logits), writes it to
+ * `logits`, and the last block to finish samples every row with the
+ * sampler of q3s_sample_batch.  The logits stay in L2 between the two; the
+ * caller gets them too.  The reference computes the projection with its
+ * matmul (bf16 with f32 accumulation in an order of the library's choosing),
+ * so logits agree with it within rounding, and the sampled ids are exactly
+ * those q3s_sample_batch gives for the returned logits.
+ *
+ * sample: the rows' sampling arguments as for q3s_sample_batch (vocab,
+ * num_rows, params, seeds, subseqs, history, tokens, status, ...); its
+ * logits, dtype, row_stride, row_offsets, row_vocab, probs and masks are not
+ * used (probs / masks must be NULL).  Path statistics are not collected. */
+#define Q3S_HEAD_MAX_ROWS 16
+typedef struct q3s_head_batch {
+  const void* hidden;            /* [num_rows, hidden_size], row stride hidden_stride elements */
+  int32_t hidden_dtype;          /* Q3S_DTYPE_F32 or Q3S_DTYPE_BF16 */
+  int32_t hidden_size;           /* H, a positive multiple of 8 */
+  int64_t hidden_stride;         /* >= H */
+  const uint16_t* weight;        /* bf16 [sample.vocab, H], row-major, 16-byte aligned */
+  float* logits;                 /* out [num_rows, sample.vocab] f32 */
+  q3s_batch sample;
+} q3s_head_batch;
+
+int q3s_head_sample(q3s_context* ctx, const q3s_head_batch* batch, void* stream);
+
 /* ---- device-resident decode frame ---------------------------------------
  * The host work that follows every Sampler call of the talker and
  * code-predictor loops, done on the device: the sampled id becomes the next

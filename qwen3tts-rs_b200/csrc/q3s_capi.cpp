@@ -52,6 +52,8 @@ struct SingleRow {
 };
 
 int launch_batch(q3s_context* ctx, const q3s_batch* b, const SingleRow* row, void* stream);
+int stream_workspace(q3s_context* ctx, void* stream, size_t need, bool with_counter,
+                     unsigned char** scratch, unsigned** counter);
 
 }  // namespace
 
@@ -80,6 +82,7 @@ struct q3s_context {
     cudaStream_t stream;
     unsigned char* ptr;
     size_t bytes;
+    unsigned* counter;  // q3s_head_sample's completion counter (zeroed once)
   };
   std::mutex ws_mu;
   std::vector<Workspace> ws;
@@ -178,8 +181,10 @@ void q3s_context_destroy(q3s_context* c) {
     if (c->h_hist) cudaFreeHost(c->h_hist);
     if (c->d_hist) cudaFree(c->d_hist);
     if (c->h_out) cudaFreeHost(c->h_out);
-    for (auto& w : c->ws)
+    for (auto& w : c->ws) {
       if (w.ptr) cudaFree(w.ptr);
+      if (w.counter) cudaFree(w.counter);
+    }
   }
   delete c;
 }
@@ -209,6 +214,41 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* b, void* stream) {
 }  // extern "C"
 
 namespace {
+
+// The stream's own workspace of at least `need` bytes (grown on demand) and,
+// with `with_counter`, its zeroed completion counter: launches on one stream
+// are ordered, so they may share them; another stream gets others.
+int stream_workspace(q3s_context* ctx, void* stream, size_t need, bool with_counter,
+                     unsigned char** scratch, unsigned** counter) {
+  std::lock_guard<std::mutex> lock(ctx->ws_mu);
+  const cudaStream_t key = (cudaStream_t)stream;
+  q3s_context::Workspace* w = nullptr;
+  for (auto& x : ctx->ws)
+    if (x.stream == key) w = &x;
+  if (!w) {
+    ctx->ws.push_back(q3s_context::Workspace{key, nullptr, 0, nullptr});
+    w = &ctx->ws.back();
+  }
+  cudaError_t e;
+  if (need > w->bytes) {
+    // cudaFree waits for the device, so no launch still uses the old one.
+    if (w->ptr) cudaFree(w->ptr);
+    w->ptr = nullptr;
+    w->bytes = 0;
+    if ((e = cudaMalloc((void**)&w->ptr, need)) != cudaSuccess)
+      return cuda_fail(e, "cudaMalloc(sampler workspace)");
+    w->bytes = need;
+  }
+  if (with_counter && !w->counter) {
+    if ((e = cudaMalloc((void**)&w->counter, 256)) != cudaSuccess)
+      return cuda_fail(e, "cudaMalloc(completion counter)");
+    if ((e = cudaMemsetAsync(w->counter, 0, 256, key)) != cudaSuccess)
+      return cuda_fail(e, "cudaMemsetAsync(completion counter)");
+  }
+  *scratch = w->ptr;
+  if (counter) *counter = w->counter;
+  return Q3S_OK;
+}
 
 // The launch of a validated batch.  `row` (single-row calls of the stateful
 // sampler): the row's parameters, Philox key and counter and history length
@@ -261,31 +301,9 @@ int launch_batch(q3s_context* ctx, const q3s_batch* b, const SingleRow* row, voi
   long long blocks = (b->num_rows + warps - 1) / warps;
   if (blocks > ctx->sm_count) blocks = ctx->sm_count;
   const size_t need = (size_t)blocks * warps * q3s::sample_scratch_per_warp(a.vcap);
-  cudaError_t e;
-  {
-    // The stream's own workspace: launches on one stream are ordered, so
-    // they may share it; another stream gets another one.
-    std::lock_guard<std::mutex> lock(ctx->ws_mu);
-    const cudaStream_t key = (cudaStream_t)stream;
-    q3s_context::Workspace* w = nullptr;
-    for (auto& x : ctx->ws)
-      if (x.stream == key) w = &x;
-    if (!w) {
-      ctx->ws.push_back(q3s_context::Workspace{key, nullptr, 0});
-      w = &ctx->ws.back();
-    }
-    if (need > w->bytes) {
-      // cudaFree waits for the device, so no launch still uses the old one.
-      if (w->ptr) cudaFree(w->ptr);
-      w->ptr = nullptr;
-      w->bytes = 0;
-      if ((e = cudaMalloc((void**)&w->ptr, need)) != cudaSuccess)
-        return cuda_fail(e, "cudaMalloc(sampler workspace)");
-      w->bytes = need;
-    }
-    a.scratch = w->ptr;
-  }
-  e = q3s::launch_sample(a, (int)blocks, warps, (cudaStream_t)stream);
+  int rc = stream_workspace(ctx, stream, need, false, &a.scratch, nullptr);
+  if (rc != Q3S_OK) return rc;
+  cudaError_t e = q3s::launch_sample(a, (int)blocks, warps, (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "sample kernel launch");
   return Q3S_OK;
 }
@@ -298,6 +316,83 @@ int q3s_context_set_test_hooks(q3s_context* ctx, uint64_t stage_wait_ns, int32_t
   if (!ctx) return fail(Q3S_E_INVALID_ARGUMENT, "q3s_context_set_test_hooks: NULL context");
   ctx->test_wait_ns = stage_wait_ns;
   ctx->test_hold_refill = hold_refill ? 1 : 0;
+  return Q3S_OK;
+}
+
+int q3s_head_sample(q3s_context* ctx, const q3s_head_batch* hb, void* stream) {
+  if (!ctx || !hb) return fail(Q3S_E_INVALID_ARGUMENT, "q3s_head_sample: NULL context or batch");
+  const q3s_batch* b = &hb->sample;
+  if (b->num_rows < 0 || b->num_rows > Q3S_HEAD_MAX_ROWS)
+    return fail(Q3S_E_INVALID_ARGUMENT,
+                "q3s_head_sample: num_rows must be in [0, " + std::to_string(Q3S_HEAD_MAX_ROWS) + "]");
+  if (b->num_rows == 0) return Q3S_OK;
+  if (b->vocab < 1 || b->vocab > Q3S_MAX_VOCAB)
+    return fail(Q3S_E_INVALID_ARGUMENT, "q3s_head_sample: vocab must be in [1, 4096]");
+  if (!hb->hidden || !hb->weight || !hb->logits || !b->params || !b->tokens || !b->status)
+    return fail(Q3S_E_INVALID_ARGUMENT,
+                "q3s_head_sample: hidden, weight, logits, params, tokens and status are required");
+  if (hb->hidden_dtype != Q3S_DTYPE_F32 && hb->hidden_dtype != Q3S_DTYPE_BF16)
+    return fail(Q3S_E_INVALID_ARGUMENT, "hidden_dtype must be Q3S_DTYPE_F32 or Q3S_DTYPE_BF16");
+  if (hb->hidden_size < 8 || hb->hidden_size % 8 != 0 || hb->hidden_stride < hb->hidden_size)
+    return fail(Q3S_E_INVALID_ARGUMENT,
+                "q3s_head_sample: hidden_size must be a positive multiple of 8 and "
+                "hidden_stride >= hidden_size");
+  if (reinterpret_cast<uintptr_t>(hb->weight) % 16 != 0)
+    return fail(Q3S_E_INVALID_ARGUMENT, "q3s_head_sample: weight must be 16-byte aligned");
+  if (!b->uniform_override && (!b->seeds || !b->subseqs))
+    return fail(Q3S_E_INVALID_ARGUMENT, "seeds and subseqs are required");
+  if (b->params_stride != 0 && b->params_stride != 1)
+    return fail(Q3S_E_INVALID_ARGUMENT, "params_stride must be 0 or 1");
+  if (b->history_offsets && !b->history)
+    return fail(Q3S_E_INVALID_ARGUMENT, "history_offsets without history");
+  if (b->probs || b->masks)
+    return fail(Q3S_E_INVALID_ARGUMENT, "q3s_head_sample: no debug outputs (probs, masks)");
+  const int vcap = (b->vocab + 31) / 32 * 32;
+  if ((size_t)b->num_rows * hb->hidden_size * 4 > q3s::head_smem(vcap))
+    return fail(Q3S_E_INVALID_ARGUMENT, "q3s_head_sample: hidden rows do not fit shared memory");
+  if (q3s::head_smem(vcap) > ctx->smem_optin)
+    return fail(Q3S_E_INVALID_ARGUMENT, "vocabulary does not fit shared memory");
+  DeviceGuard g(ctx->device);
+  if (g.err != cudaSuccess) return cuda_fail(g.err, "cudaSetDevice");
+  q3s::KernelArgs a;
+  a.logits = hb->logits;
+  a.dtype = Q3S_DTYPE_F32;
+  a.vocab = b->vocab;
+  a.num_rows = b->num_rows;
+  a.row_stride = b->vocab;
+  a.row_offsets = nullptr;
+  a.row_vocab = nullptr;
+  a.params = b->params;
+  a.params_stride = b->params_stride;
+  a.seeds = reinterpret_cast<const unsigned long long*>(b->seeds);
+  a.subseqs = reinterpret_cast<const unsigned long long*>(b->subseqs);
+  a.history = b->history;
+  a.history_offsets = reinterpret_cast<const long long*>(b->history_offsets);
+  a.history_ends = b->history_offsets ? reinterpret_cast<const long long*>(b->history_ends)
+                                      : nullptr;
+  a.tokens = b->tokens;
+  a.status = b->status;
+  a.uniform_override = b->uniform_override;
+  a.probs = nullptr;
+  a.masks = nullptr;
+  a.probs_stride = 0;
+  if (ctx->test_wait_ns) a.wait_ns = ctx->test_wait_ns;
+  a.vcap = vcap;
+  q3s::HeadArgs h;
+  h.hidden = hb->hidden;
+  h.hidden_dtype = hb->hidden_dtype;
+  h.hidden_size = hb->hidden_size;
+  h.hidden_stride = hb->hidden_stride;
+  h.weight = hb->weight;
+  h.vocab = b->vocab;
+  h.logits = hb->logits;
+  long long grid = (b->vocab + 15) / 16;
+  if (grid > ctx->sm_count) grid = ctx->sm_count;
+  int rc = stream_workspace(ctx, stream, (size_t)16 * q3s::sample_scratch_per_warp(vcap), true,
+                            &a.scratch, &h.counter);
+  if (rc != Q3S_OK) return rc;
+  const cudaError_t e = q3s::launch_head_sample(h, a, (int)grid, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "head sample kernel launch");
   return Q3S_OK;
 }
 

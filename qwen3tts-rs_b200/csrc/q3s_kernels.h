@@ -51,7 +51,22 @@ struct KernelArgs {
   long long row_hist_len = 0;
 };
 
+// The head projection of q3s_head_sample (logits = hidden · weightᵀ).
+struct HeadArgs {
+  const void* hidden;      // [rows, hidden_size], row stride hidden_stride elements
+  int hidden_dtype;        // Q3S_DTYPE_F32 or Q3S_DTYPE_BF16
+  int hidden_size;         // a multiple of 8
+  long long hidden_stride;
+  const unsigned short* weight;  // bf16 [vocab, hidden_size], 16-byte aligned
+  int vocab;
+  float* logits;           // out [rows, vocab]
+  unsigned* counter;       // blocks done; 0 before the launch, 0 again after it
+};
+
 size_t sample_smem_per_warp(int vcap, int dtype);
+size_t head_smem(int vcap);
+cudaError_t launch_head_sample(const HeadArgs& h, const KernelArgs& a, int grid,
+                               cudaStream_t stream);
 size_t sample_scratch_per_warp(int vcap);
 int sample_max_warps(int vcap, int dtype, size_t smem_limit);
 cudaError_t launch_sample(const KernelArgs& a, int grid, int warps, cudaStream_t stream);

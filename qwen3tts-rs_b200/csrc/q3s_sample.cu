@@ -2343,9 +2343,13 @@ general:
   return {(int)(r >> 32), (uint32_t)r};
 }
 
+// The body of a sampling block: block `bid` of `G` blocks that stride over
+// the rows, in the dynamic shared memory `smem` (block_smem bytes).  The
+// sampling kernel runs it with its own block index; the fused head kernel's
+// last block runs it as the one block of a one-block grid.
 template <int DT, int NJ, bool DBG, bool RT>
-__global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelArgs a) {
-  extern __shared__ __align__(128) unsigned char smem[];
+__device__ __forceinline__ void sample_block(const KernelArgs& a, unsigned char* smem,
+                                             const long long bid, const long long G) {
   constexpr int es = Elem<DT>::BYTES;
   const int warp = threadIdx.x >> 5;
   const int warps = blockDim.x >> 5;
@@ -2355,9 +2359,8 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
   const size_t sbytes = stage_bytes(a.vcap, es);
   unsigned char* ring = smem + HEAD_BYTES;
   FastSpace f = carve_warp(ring + RING * sbytes + (size_t)warp * warp_bytes(a.vcap), a.vcap);
-  const long long gw = (long long)blockIdx.x * warps + warp;
+  const long long gw = bid * warps + warp;
   const GenSpace g = carve_gen(a.scratch + (size_t)gw * gen_bytes(a.vcap), a.vcap);
-  const long long G = gridDim.x;
   if (threadIdx.x == 0) {
     for (int s = 0; s < RING; ++s) {
       mbar_init(&ctl->full[s], 1);
@@ -2369,7 +2372,7 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
     fence_mbarrier_init();
     fence_proxy_async_smem();
     for (int s = 0; s < RING; ++s) {
-      const long long row = blockIdx.x + (long long)s * G;
+      const long long row = bid + (long long)s * G;
       if (row < a.num_rows) {
         issue_row<DT>(a, row, ring + s * sbytes, &ctl->full[s]);
         ctl->issued[s] = 1u;
@@ -2380,7 +2383,7 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
   for (int i = threadIdx.x; i < PLAN_SLOTS; i += blockDim.x)
     reinterpret_cast<volatile uint32_t*>(&plans[i])[7] = NO_TAG;
   if (threadIdx.x < 64) {
-    const long long row = blockIdx.x + (long long)threadIdx.x * G;
+    const long long row = bid + (long long)threadIdx.x * G;
     if (row < a.num_rows) store_plan(&plans[threadIdx.x], compute_plan(a, row, threadIdx.x));
   }
   __syncthreads();
@@ -2390,18 +2393,18 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
     uint32_t t = 0;
     if (lane == 0) t = atomicAdd(&ctl->ticket, 1u);
     t = __shfl_sync(FULL, t, 0);
-    const long long row = blockIdx.x + (long long)t * G;
+    const long long row = bid + (long long)t * G;
     if (row >= a.num_rows) break;
     const long long clk0 = DBG ? clock64() : 0;
     const int slot = (int)(t % RING);
     const uint32_t gen = t / RING;
     f.stage = ring + slot * sbytes;
-    Releaser rel{&a, ctl, f.stage, slot, blockIdx.x + (long long)(t + RING) * G, gen + 1u, false};
+    Releaser rel{&a, ctl, f.stage, slot, bid + (long long)(t + RING) * G, gen + 1u, false};
     // The warp that opens a batch of 32 tickets plans the batch after it,
     // one lane per ticket.
     if ((t & 31u) == 0u && t >= 32u) {
       const uint32_t tp = t + 32u + lane;
-      const long long prow = blockIdx.x + (long long)tp * G;
+      const long long prow = bid + (long long)tp * G;
       if (prow < a.num_rows) store_plan(&plans[tp % PLAN_SLOTS], compute_plan(a, prow, tp));
     }
     RowPlan pl;
@@ -2466,6 +2469,104 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelA
     for (int s = 0; s < RING; ++s)
       if (ctl->issued[s] > ctl->consumed[s])
         mbar_wait_bounded(&ctl->full[s], ctl->consumed[s] & 1u, WAIT_LIMIT_NS);
+}
+
+template <int DT, int NJ, bool DBG, bool RT>
+__global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  sample_block<DT, NJ, DBG, RT>(a, smem, blockIdx.x, gridDim.x);
+}
+
+// Producer fusion: the head projection logits = hidden · Wᵀ of the talker's
+// codec_head (talker.rs:87-89) or a code-predictor lm_head
+// (code_predictor.rs:402), then the sampling of its rows, in one launch.
+// Every block stages the (at most MAX_WARPS) hidden rows as f32 in shared
+// memory and computes a slice of the outputs, one warp per output: each lane
+// reads 16-byte vectors of the weight row, multiplies by the hidden values
+// (bf16 x f32, each product and sum rounded separately) and the lanes' partial
+// sums are combined by a fixed butterfly, so every launch computes the same
+// f32 logits.  The logits go to the caller's buffer, where they stay in L2.
+// The last block to finish its slice (a device-scope counter, reset by that
+// block) runs the sampling block over all rows, one warp per row.
+template <int NJ>
+__global__ void __launch_bounds__(MAX_WARPS * 32, 1)
+    head_sample_kernel(const HeadArgs h, const KernelArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int last_block;
+  const int R = (int)a.num_rows;
+  const int H = h.hidden_size;
+  float* hs = reinterpret_cast<float*>(smem);  // [R, H]
+  for (int i = threadIdx.x; i < R * H; i += blockDim.x) {
+    const int r = i / H, k = i - r * H;
+    const long long off = (long long)r * h.hidden_stride + k;
+    hs[i] = h.hidden_dtype == Q3S_DTYPE_F32
+                ? static_cast<const float*>(h.hidden)[off]
+                : __uint_as_float((uint32_t)static_cast<const uint16_t*>(h.hidden)[off] << 16);
+  }
+  __syncthreads();
+  const int lane = (int)lane_id();
+  const int warps = blockDim.x >> 5;
+  const long long nw = (long long)gridDim.x * warps;
+  const int Q = H >> 3;  // 16-byte weight vectors per row
+  for (long long v = (long long)blockIdx.x * warps + (threadIdx.x >> 5); v < h.vocab; v += nw) {
+    const uint4* wrow = reinterpret_cast<const uint4*>(h.weight + v * H);
+    float acc[MAX_WARPS];
+#pragma unroll
+    for (int r = 0; r < MAX_WARPS; ++r) acc[r] = 0.0f;
+    for (int q = lane; q < Q; q += 32) {
+      const uint4 w4 = __ldg(wrow + q);
+      const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+      float wv[8];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        wv[2 * t] = __uint_as_float(ww[t] << 16);
+        wv[2 * t + 1] = __uint_as_float(ww[t] & 0xFFFF0000u);
+      }
+#pragma unroll
+      for (int r = 0; r < MAX_WARPS; ++r) {
+        if (r < R) {
+          const float4 h0 = *reinterpret_cast<const float4*>(hs + r * H + 8 * q);
+          const float4 h1 = *reinterpret_cast<const float4*>(hs + r * H + 8 * q + 4);
+          float s2 = acc[r];
+          s2 = __fadd_rn(s2, __fmul_rn(wv[0], h0.x));
+          s2 = __fadd_rn(s2, __fmul_rn(wv[1], h0.y));
+          s2 = __fadd_rn(s2, __fmul_rn(wv[2], h0.z));
+          s2 = __fadd_rn(s2, __fmul_rn(wv[3], h0.w));
+          s2 = __fadd_rn(s2, __fmul_rn(wv[4], h1.x));
+          s2 = __fadd_rn(s2, __fmul_rn(wv[5], h1.y));
+          s2 = __fadd_rn(s2, __fmul_rn(wv[6], h1.z));
+          s2 = __fadd_rn(s2, __fmul_rn(wv[7], h1.w));
+          acc[r] = s2;
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < MAX_WARPS; ++r) {
+      if (r < R) {
+        float x = acc[r];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) x = __fadd_rn(x, __shfl_xor_sync(FULL, x, o));
+        if (lane == r) h.logits[(long long)r * h.vocab + v] = x;
+      }
+    }
+  }
+  // Completion: every block publishes its slice, the last one samples.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(h.counter, 1u);
+    last_block = prev == gridDim.x - 1u;
+    if (last_block) {
+      __threadfence();       // the other blocks' logits are visible from here on
+      *h.counter = 0u;       // ready for the next launch on this stream
+    }
+  }
+  __syncthreads();
+  if (!last_block) return;
+  // The sampling block reads the logits with bulk copies (the async proxy).
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  __syncthreads();
+  sample_block<Q3S_DTYPE_F32, NJ, false, false>(a, smem, 0, 1);
 }
 
 // Greedy argmax rows (sampling.rs:40-60 and :72-117), one warp per row.
@@ -2587,6 +2688,34 @@ cudaError_t launch_sample(const KernelArgs& a, int grid, int warps, cudaStream_t
   }
   if (chunk_vectors(a.vcap, 2) == 8) return launch_t<Q3S_DTYPE_BF16, 8>(a, grid, warps, stream);
   return launch_t<Q3S_DTYPE_BF16, 16>(a, grid, warps, stream);
+}
+
+size_t head_smem(int vcap) { return block_smem(vcap, 4, MAX_WARPS); }
+
+cudaError_t launch_head_sample(const HeadArgs& h, const KernelArgs& a, int grid,
+                               cudaStream_t stream) {
+  const size_t smem = block_smem(a.vcap, 4, MAX_WARPS);
+  static std::atomic<int> smem_set[4][MAX_DEVICES];
+  cudaError_t e;
+  switch (chunk_vectors(a.vcap, 4)) {
+    case 8:
+      if ((e = ensure_smem(head_sample_kernel<8>, smem_set[0], smem)) != cudaSuccess) return e;
+      head_sample_kernel<8><<<grid, MAX_WARPS * 32, smem, stream>>>(h, a);
+      break;
+    case 16:
+      if ((e = ensure_smem(head_sample_kernel<16>, smem_set[1], smem)) != cudaSuccess) return e;
+      head_sample_kernel<16><<<grid, MAX_WARPS * 32, smem, stream>>>(h, a);
+      break;
+    case 24:
+      if ((e = ensure_smem(head_sample_kernel<24>, smem_set[2], smem)) != cudaSuccess) return e;
+      head_sample_kernel<24><<<grid, MAX_WARPS * 32, smem, stream>>>(h, a);
+      break;
+    default:
+      if ((e = ensure_smem(head_sample_kernel<32>, smem_set[3], smem)) != cudaSuccess) return e;
+      head_sample_kernel<32><<<grid, MAX_WARPS * 32, smem, stream>>>(h, a);
+      break;
+  }
+  return cudaGetLastError();
 }
 
 cudaError_t launch_greedy(const void* logits, int dtype, long long num_rows, long long row_stride,

@@ -95,6 +95,14 @@ class _Batch(ctypes.Structure):
     ]
 
 
+class _HeadBatch(ctypes.Structure):
+    _fields_ = [
+        ("hidden", ctypes.c_void_p), ("hidden_dtype", ctypes.c_int32),
+        ("hidden_size", ctypes.c_int32), ("hidden_stride", ctypes.c_int64),
+        ("weight", ctypes.c_void_p), ("logits", ctypes.c_void_p), ("sample", _Batch),
+    ]
+
+
 class _SessionConfig(ctypes.Structure):
     _fields_ = [
         ("id", ctypes.c_uint64), ("seed", ctypes.c_uint64), ("subseq", ctypes.c_uint64),
@@ -147,7 +155,10 @@ EXPORTED_SYMBOLS = (
     "q3s_commit_rows", "q3s_scheduler_create", "q3s_scheduler_destroy", "q3s_scheduler_add",
     "q3s_scheduler_cancel", "q3s_scheduler_begin_frame", "q3s_scheduler_step",
     "q3s_scheduler_end_frame", "q3s_scheduler_codes", "q3s_scheduler_session_state",
+    "q3s_head_sample",
 )
+
+HEAD_MAX_ROWS = 16
 
 # Row paths of the sampling kernel (Q3S_PATH_* of include/q3s_sampler.h).
 PATH_NAMES = (
@@ -188,6 +199,7 @@ def load(path: Optional[os.PathLike] = None):
                                           ctypes.c_void_p]
     L.q3s_embed_sum.argtypes = [ctypes.c_void_p, ctypes.POINTER(_EmbedBatch), ctypes.c_void_p]
     L.q3s_commit_rows.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Commit), ctypes.c_void_p]
+    L.q3s_head_sample.argtypes = [ctypes.c_void_p, ctypes.POINTER(_HeadBatch), ctypes.c_void_p]
     L.q3s_scheduler_create.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
                                        ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p)]
     L.q3s_scheduler_destroy.argtypes = [ctypes.c_void_p]
@@ -856,3 +868,67 @@ class Scheduler:
             self.close()
         except Exception:
             pass
+
+
+def head_sample(hidden, weight, params, seeds=None, subseqs=None, *, history=None,
+                history_offsets=None, history_ends=None, uniform_override=None,
+                ctx: Optional[Context] = None, stream=None, out=None):
+    """The head projection logits = hidden · weightᵀ and the sampling of its
+    rows in one launch (q3s_head_sample).  hidden: CUDA [R, H] float32 or
+    bfloat16 (R <= HEAD_MAX_ROWS, H a multiple of 8); weight: CUDA bfloat16
+    [V, H], contiguous.  The sampling arguments are those of sample_batch.
+    Returns (tokens int32 [R], status uint8 [R], logits float32 [R, V])."""
+    import torch
+    if hidden.dim() != 2 or hidden.stride(1) != 1:
+        raise ValueError("hidden must be [R, H] with contiguous rows")
+    if weight.dtype != torch.bfloat16 or weight.dim() != 2 or not weight.is_contiguous():
+        raise ValueError("weight must be a contiguous bfloat16 [V, H] tensor")
+    R, H = int(hidden.shape[0]), int(hidden.shape[1])
+    V = int(weight.shape[0])
+    if int(weight.shape[1]) != H:
+        raise ValueError("weight and hidden disagree on H")
+    if hidden.device != weight.device:
+        raise ValueError("hidden and weight must be on one device")
+    dev = hidden.device
+    if hidden.dtype == torch.float32:
+        hdt = DTYPE_F32
+    elif hidden.dtype == torch.bfloat16:
+        hdt = DTYPE_BF16
+    else:
+        raise TypeError("hidden must be float32 or bfloat16")
+    if isinstance(params, np.ndarray):
+        params = torch.from_numpy(params.view(np.uint8).copy()).to(dev)
+    nparams = params.numel() // ROW_PARAMS_DTYPE.itemsize
+    if nparams not in (1, R):
+        raise ValueError("params must hold 1 or R records")
+    ctx = ctx or default_context(dev.index)
+    if out is None:
+        tokens = torch.empty(R, dtype=torch.int32, device=dev)
+        status = torch.empty(R, dtype=torch.uint8, device=dev)
+        logits = torch.empty((R, V), dtype=torch.float32, device=dev)
+    else:
+        tokens, status, logits = out
+    hb = _HeadBatch()
+    hb.hidden = hidden.data_ptr()
+    hb.hidden_dtype = hdt
+    hb.hidden_size = H
+    hb.hidden_stride = hidden.stride(0)
+    hb.weight = weight.data_ptr()
+    hb.logits = logits.data_ptr()
+    b = hb.sample
+    b.vocab = V
+    b.num_rows = R
+    b.params = params.data_ptr()
+    b.params_stride = 0 if nparams == 1 else 1
+    b.seeds = _dptr(seeds)
+    b.subseqs = _dptr(subseqs)
+    b.history = _dptr(history)
+    b.history_offsets = _dptr(history_offsets)
+    b.history_ends = _dptr(history_ends)
+    b.tokens = tokens.data_ptr()
+    b.status = status.data_ptr()
+    b.uniform_override = _dptr(uniform_override)
+    s = torch.cuda.current_stream(dev).cuda_stream if stream is None else stream
+    _check(load().q3s_head_sample(ctx.handle, ctypes.byref(hb), ctypes.c_void_p(s)),
+           "q3s_head_sample")
+    return tokens, status, logits

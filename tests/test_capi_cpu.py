@@ -67,14 +67,15 @@ def test_struct_layouts_match_binding(tmp_path):
 #include <stdio.h>
 #include "q3s_sampler.h"
 int main(void) {
-  printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\n", sizeof(q3s_row_params),
+  printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\n", sizeof(q3s_row_params),
          offsetof(q3s_row_params, top_k), offsetof(q3s_row_params, do_sample),
          offsetof(q3s_row_params, suppress_from), offsetof(q3s_row_params, allow_token),
          offsetof(q3s_row_params, ctr_lo), sizeof(q3s_batch), offsetof(q3s_batch, probs_stride),
          sizeof(q3s_sampling_options), sizeof(q3s_sampler_diagnostics),
          sizeof(q3s_embed_batch), offsetof(q3s_embed_batch, text_stride),
          offsetof(q3s_embed_batch, status), offsetof(q3s_batch, history_ends),
-         sizeof(q3s_commit), offsetof(q3s_commit, group), offsetof(q3s_commit, history_limits));
+         sizeof(q3s_commit), offsetof(q3s_commit, group), offsetof(q3s_commit, history_limits),
+         sizeof(q3s_head_batch), offsetof(q3s_head_batch, sample));
   return 0;
 }
 ''')
@@ -91,7 +92,8 @@ int main(void) {
                    ctypes.sizeof(q3s._Diagnostics), ctypes.sizeof(q3s._EmbedBatch),
                    q3s._EmbedBatch.text_stride.offset, q3s._EmbedBatch.status.offset,
                    q3s._Batch.history_ends.offset, ctypes.sizeof(q3s._Commit),
-                   q3s._Commit.group.offset, q3s._Commit.history_limits.offset]
+                   q3s._Commit.group.offset, q3s._Commit.history_limits.offset,
+                   ctypes.sizeof(q3s._HeadBatch), q3s._HeadBatch.sample.offset]
 
 
 def test_context_without_device_fails_cleanly():
