@@ -184,3 +184,61 @@ def test_frames_with_failures_history_and_embedding():
             emb[torch.from_numpy(ok).to(DEV)].view(torch.int16).cpu().numpy(),
             ref.view(np.int16))
         assert not ref_st.any()
+
+
+def test_code_predictor_frame_replays_from_a_cuda_graph():
+    """The 15 code-predictor groups of a frame (sampling launch + device-side
+    commit each) captured once in a CUDA graph: a replay from the same
+    counters gives the codes, counters and statuses of the eager frame."""
+    S, G = 64, 15
+    rng = np.random.default_rng(5)
+    x = torch.from_numpy((rng.standard_normal((G, S, 2048)) * 3.0).astype(np.float32))
+    x = x.to(torch.bfloat16).to(DEV)
+    p = q3s.make_params(1, temperature=0.9, top_k=50, top_p=1.0, repetition_penalty=1.0)
+    pd = torch.from_numpy(p.view(np.uint8).copy()).to(DEV)
+    seeds = torch.from_numpy(rng.integers(0, 2**63, S).astype(np.int64)).to(DEV)
+    sub0 = torch.from_numpy(rng.integers(0, 1000, S).astype(np.int64)).to(DEV)
+    ctx = q3s.Context(0)
+
+    def frame(subseqs, codes, fstat, stream):
+        tok = torch.empty(S, dtype=torch.int32, device=DEV)
+        st = torch.empty(S, dtype=torch.uint8, device=DEV)
+        launches = [q3s.prepare_batch(x[g], pd, seeds, subseqs, ctx=ctx, out=(tok, st))
+                    for g in range(G)]
+        def run():
+            fstat.zero_()
+            for g in range(G):
+                launches[g](stream.cuda_stream)
+                q3s.commit_rows(tok, st, params=pd, subseqs=subseqs, codes=codes, group=g + 1,
+                                frame_status=fstat, ctx=ctx, stream=stream.cuda_stream)
+        return run, (tok, st, launches)
+
+    s = torch.cuda.Stream(DEV)
+    # Eager frame.
+    sub_e = sub0.clone()
+    codes_e = torch.zeros((S, 16), dtype=torch.int32, device=DEV)
+    fstat_e = torch.zeros(S, dtype=torch.uint8, device=DEV)
+    run_e, keep_e = frame(sub_e, codes_e, fstat_e, s)
+    with torch.cuda.stream(s):
+        run_e()
+    torch.cuda.synchronize()
+    # The same frame captured (after one warm run on its own buffers).
+    sub_g = sub0.clone()
+    codes_g = torch.zeros((S, 16), dtype=torch.int32, device=DEV)
+    fstat_g = torch.zeros(S, dtype=torch.uint8, device=DEV)
+    run_g, keep_g = frame(sub_g, codes_g, fstat_g, s)
+    with torch.cuda.stream(s):
+        run_g()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        run_g()
+    sub_g.copy_(sub0)
+    codes_g.zero_()
+    torch.cuda.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(codes_g, codes_e)
+    assert torch.equal(sub_g, sub_e)
+    assert torch.equal(fstat_g, fstat_e) and int(fstat_g.sum()) == 0
+    assert torch.equal(sub_e, sub0 + G)
