@@ -267,11 +267,15 @@ int q3s_scheduler_add(q3s_scheduler* q, const q3s_session_config* c) {
   if (live(q, c->id))
     return sched_fail(Q3S_E_INVALID_ARGUMENT,
                       "q3s_scheduler_add: session " + std::to_string(c->id) + " already added");
+  // Sessions leaving at the next frame boundary: cancelled or failed (a slot
+  // that is both counts once).
   long long leaving = 0;
-  for (uint64_t id : q->cancels)
-    for (uint64_t x : q->ids)
-      if (x == id) ++leaving;
-  for (uint8_t f : q->failed) leaving += f ? 1 : 0;
+  for (size_t i = 0; i < q->ids.size(); ++i) {
+    bool out = i < q->failed.size() && q->failed[i];
+    for (uint64_t id : q->cancels)
+      if (q->ids[i] == id) out = true;
+    leaving += out ? 1 : 0;
+  }
   if ((long long)q->ids.size() - leaving + (long long)q->adds.size() + 1 > q->M)
     return sched_fail(Q3S_E_INVALID_ARGUMENT,
                       "q3s_scheduler_add: all " + std::to_string(q->M) + " sessions are in use");
@@ -344,8 +348,11 @@ int q3s_scheduler_begin_frame(q3s_scheduler* q, uint64_t* ids, int32_t cap, int3
     q3s::sched::move_kernel<<<nm, 256, 0, st>>>(q->s, q->d_moves);
     if ((e = cudaGetLastError()) != cudaSuccess) return q3s::record_cuda_error(e, "move kernel");
   }
-  // Joining sessions take the slots after the staying ones.
+  // Joining sessions take the slots after the staying ones (add() keeps
+  // their number within the slots; checked again before any slot is written).
   const int na = (int)q->adds.size();
+  if ((long long)q->ids.size() + na > q->M)
+    return sched_fail(Q3S_E_INVALID_ARGUMENT, "q3s_scheduler_begin_frame: more sessions than slots");
   if (na > 0) {
     long long off = 0;
     for (int k = 0; k < na; ++k) {

@@ -184,3 +184,25 @@ def test_scheduler_rejects_misuse():
     sched.cancel(1)
     assert sched.begin_frame() == [2]
     sched.close()
+
+
+def test_capacity_counts_a_cancelled_failed_session_once():
+    """A session that fails in a frame and is also cancelled frees one slot:
+    with two slots, one session staying and that one leaving, one add fits
+    and a second is refused."""
+    T = q3s.SamplingOptions
+    sched = q3s.Scheduler(max_sessions=2, groups=G, history_capacity=8)
+    o = T(0.9, 50, 1.0, 1.0)
+    sched.add(1, 7, o, o)
+    sched.add(2, 8, T(0.9, 50, 1.5, 1.0), o)       # invalid top_p: fails at its first call
+    ids, codes, status = run_frame(sched, 0)
+    assert dict(zip(ids, status.tolist()))[2] == q3s.STATUS_INVALID_TOP_P
+    sched.cancel(2)
+    sched.add(3, 9, o, o)
+    with pytest.raises(q3s.LibraryError):
+        sched.add(4, 10, o, o)
+    assert sorted(sched.begin_frame()) == [1, 3]
+    for g in range(G):
+        sched.step(g, torch.zeros((2, TALKER_V if g == 0 else CP_V), device=DEV))
+    sched.end_frame()
+    sched.close()
