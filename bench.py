@@ -625,15 +625,13 @@ def secondary(ctx, dev, q3s, workloads, np, torch):
     fstat_f = torch.zeros(64, dtype=torch.uint8, device=dev)
     tok_f = torch.empty(64, dtype=torch.int32, device=dev)
     st_f = torch.empty(64, dtype=torch.uint8, device=dev)
-    glaunch = [q3s.prepare_batch(x[g], pc, seeds_f, sub_f, ctx=ctx, out=(tok_f, st_f))
-               for g in range(15)]
 
     def dev_frame():
         fstat_f.zero_()
         for g in range(15):
-            glaunch[g](cs.cuda_stream)
-            q3s.commit_rows(tok_f, st_f, params=pc, subseqs=sub_f, codes=codes_f, group=g + 1,
-                            frame_status=fstat_f, ctx=ctx, stream=cs.cuda_stream)
+            q3s.sample_commit(x[g], pc, seeds_f, sub_f, codes=codes_f, group=g + 1,
+                              frame_status=fstat_f, ctx=ctx, stream=cs.cuda_stream,
+                              out=(tok_f, st_f))
     with torch.cuda.stream(cs):
         dev_frame()
     torch.cuda.synchronize()
@@ -647,7 +645,8 @@ def secondary(ctx, dev, q3s, workloads, np, torch):
         raise RuntimeError("device-resident frame failed")
     out["cp_frame_64x15_device_resident"] = {
         "us_per_group_eager": ms_eager * 1e3 / 15, "us_per_group_cuda_graph": ms_graph * 1e3 / 15,
-        "note": "15 x (sampling launch + q3s_commit_rows), ids and counters kept on the device; "
+        "note": "15 x q3s_sample_commit (sampling and commit in one launch), ids and counters "
+                "kept on the device; "
                 "eager launches against one CUDA graph replay per frame; L2 flushed per frame"}
     del graph
     # Codebook embedding sum after sampling: 4096 streams, 16 codebooks

@@ -322,6 +322,16 @@ typedef struct q3s_commit {
 
 int q3s_commit_rows(q3s_context* ctx, const q3s_commit* commit, void* stream);
 
+/* q3s_sample_batch followed by q3s_commit_rows, in one launch: each row's
+ * warp commits the row right after storing its result.  `commit`'s
+ * num_rows, params, params_stride, tokens and status are not read (the
+ * batch's are used); its other fields are as for q3s_commit_rows.  Rows are
+ * the batch's rows, so `subseqs` is usually the batch's own subseqs array
+ * and the history fields the batch's history, history_ends and a limits
+ * array. */
+int q3s_sample_commit(q3s_context* ctx, const q3s_batch* batch, const q3s_commit* commit,
+                      void* stream);
+
 /* ---- continuous batching of sessions ------------------------------------
  * The scheduler the reference plans for many concurrent synthesis sessions
  * (tasks/P12-c-abi-and-continuous-batching.md:11-16: P12-T03 per-session

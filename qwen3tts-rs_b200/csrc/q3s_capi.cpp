@@ -51,7 +51,9 @@ struct SingleRow {
   long long hist_len;
 };
 
-int launch_batch(q3s_context* ctx, const q3s_batch* b, const SingleRow* row, void* stream);
+int launch_batch(q3s_context* ctx, const q3s_batch* b, const SingleRow* row, void* stream,
+                 const q3s_commit* commit = nullptr);
+int validate_batch(const q3s_batch* b);
 int stream_workspace(q3s_context* ctx, void* stream, size_t need, bool with_counter,
                      unsigned char** scratch, unsigned** counter);
 
@@ -193,6 +195,31 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* b, void* stream) {
   if (!ctx || !b) return fail(Q3S_E_INVALID_ARGUMENT, "q3s_sample_batch: NULL context or batch");
   if (b->num_rows < 0) return fail(Q3S_E_INVALID_ARGUMENT, "num_rows must be >= 0");
   if (b->num_rows == 0) return Q3S_OK;
+  const int rc = validate_batch(b);
+  if (rc != Q3S_OK) return rc;
+  return launch_batch(ctx, b, nullptr, stream);
+}
+
+int q3s_sample_commit(q3s_context* ctx, const q3s_batch* b, const q3s_commit* c, void* stream) {
+  if (!ctx || !b || !c)
+    return fail(Q3S_E_INVALID_ARGUMENT, "q3s_sample_commit: NULL context, batch or commit");
+  if (b->num_rows < 0) return fail(Q3S_E_INVALID_ARGUMENT, "num_rows must be >= 0");
+  if (b->num_rows == 0) return Q3S_OK;
+  int rc = validate_batch(b);
+  if (rc != Q3S_OK) return rc;
+  if (c->codes && (c->group < 0 || c->codes_stride <= c->group))
+    return fail(Q3S_E_INVALID_ARGUMENT, "q3s_sample_commit: group outside codes_stride");
+  if (c->history && (!c->history_ends || !c->history_limits))
+    return fail(Q3S_E_INVALID_ARGUMENT,
+                "q3s_sample_commit: history needs history_ends and history_limits");
+  return launch_batch(ctx, b, nullptr, stream, c);
+}
+
+}  // extern "C"
+
+namespace {
+
+int validate_batch(const q3s_batch* b) {
   if (b->dtype != Q3S_DTYPE_F32 && b->dtype != Q3S_DTYPE_BF16)
     return fail(Q3S_E_INVALID_ARGUMENT, "dtype must be Q3S_DTYPE_F32 or Q3S_DTYPE_BF16");
   if (b->vocab < 0) return fail(Q3S_E_INVALID_ARGUMENT, "vocab must be >= 0");
@@ -208,12 +235,8 @@ int q3s_sample_batch(q3s_context* ctx, const q3s_batch* b, void* stream) {
     return fail(Q3S_E_INVALID_ARGUMENT, "history_offsets without history");
   if ((b->probs || b->masks) && b->probs_stride < b->vocab)
     return fail(Q3S_E_INVALID_ARGUMENT, "probs_stride must be >= vocab");
-  return launch_batch(ctx, b, nullptr, stream);
+  return Q3S_OK;
 }
-
-}  // extern "C"
-
-namespace {
 
 // The stream's own workspace of at least `need` bytes (grown on demand) and,
 // with `with_counter`, its zeroed completion counter: launches on one stream
@@ -254,7 +277,8 @@ int stream_workspace(q3s_context* ctx, void* stream, size_t need, bool with_coun
 // sampler): the row's parameters, Philox key and counter and history length
 // travel in the kernel arguments instead of b->params / seeds / subseqs /
 // history_offsets.
-int launch_batch(q3s_context* ctx, const q3s_batch* b, const SingleRow* row, void* stream) {
+int launch_batch(q3s_context* ctx, const q3s_batch* b, const SingleRow* row, void* stream,
+                 const q3s_commit* commit) {
   DeviceGuard g(ctx->device);
   if (g.err != cudaSuccess) return cuda_fail(g.err, "cudaSetDevice");
   q3s::KernelArgs a;
@@ -282,6 +306,17 @@ int launch_batch(q3s_context* ctx, const q3s_batch* b, const SingleRow* row, voi
   if (ctx->test_wait_ns) a.wait_ns = ctx->test_wait_ns;
   a.hold_refill = ctx->test_hold_refill;
   a.path_stats = ctx->path_stats;
+  if (commit) {
+    a.commit = 1;
+    a.c_codes = commit->codes;
+    a.c_codes_stride = commit->codes_stride;
+    a.c_group = commit->group;
+    a.c_frame_status = commit->frame_status;
+    a.c_subseqs = reinterpret_cast<unsigned long long*>(commit->subseqs);
+    a.c_history = commit->history;
+    a.c_history_ends = reinterpret_cast<long long*>(commit->history_ends);
+    a.c_history_limits = reinterpret_cast<const long long*>(commit->history_limits);
+  }
   if (row) {
     a.inline_row = 1;
     a.row_params = row->params;

@@ -49,6 +49,18 @@ struct KernelArgs {
   q3s_row_params row_params{};
   unsigned long long row_seed = 0, row_subseq = 0;
   long long row_hist_len = 0;
+  // In-kernel commit (q3s_sample_commit): after storing a row's result, its
+  // warp does what q3s_commit_rows does for the row.  subseqs / history /
+  // history_ends are the launch's own arrays, written for this row only.
+  int commit = 0;
+  unsigned* c_codes = nullptr;
+  long long c_codes_stride = 0;
+  int c_group = 0;
+  unsigned char* c_frame_status = nullptr;
+  unsigned long long* c_subseqs = nullptr;
+  unsigned short* c_history = nullptr;
+  long long* c_history_ends = nullptr;
+  const long long* c_history_limits = nullptr;
 };
 
 // The head projection of q3s_head_sample (logits = hidden · weightᵀ).

@@ -2343,6 +2343,28 @@ general:
   return {(int)(r >> 32), (uint32_t)r};
 }
 
+// The commit of one row (the per-row statements of q3s_commit_rows): the id
+// into the frame's code column; unless the row's frame already failed, the
+// subsequence advanced on a draw, the id appended to the row's history range
+// (HISTORY_FULL when it has no room) and the first failure kept.
+__device__ __noinline__ void commit_row(const KernelArgs& a, long long row, RowOut out,
+                                        bool do_sample) {
+  if (a.c_codes) a.c_codes[row * a.c_codes_stride + a.c_group] = out.token;
+  if (a.c_frame_status && a.c_frame_status[row] != Q3S_STATUS_OK) return;
+  int st = out.status;
+  if (st == Q3S_STATUS_OK && a.c_subseqs && do_sample) a.c_subseqs[row] += 1;
+  if (st == Q3S_STATUS_OK && a.c_history) {
+    const long long e = a.c_history_ends[row];
+    if (e < a.c_history_limits[row]) {
+      a.c_history[e] = (unsigned short)out.token;
+      a.c_history_ends[row] = e + 1;
+    } else {
+      st = Q3S_STATUS_HISTORY_FULL;
+    }
+  }
+  if (a.c_frame_status) a.c_frame_status[row] = (unsigned char)st;
+}
+
 // The body of a sampling block: block `bid` of `G` blocks that stride over
 // the rows, in the dynamic shared memory `smem` (block_smem bytes).  The
 // sampling kernel runs it with its own block index; the fused head kernel's
@@ -2455,6 +2477,7 @@ __device__ __forceinline__ void sample_block(const KernelArgs& a, unsigned char*
     if (lane == 0) {
       a.tokens[row] = out.token;
       a.status[row] = (unsigned char)out.status;
+      if (a.commit) commit_row(a, row, out, (pflags & PF_DO_SAMPLE) != 0u);
       if (DBG && a.path_stats) {
         atomicAdd(&a.path_stats[path], 1ull);
         atomicAdd(&a.path_stats[Q3S_PATH_COUNT + path], (unsigned long long)(clock64() - clk0));

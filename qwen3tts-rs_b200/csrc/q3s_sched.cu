@@ -16,8 +16,9 @@
 // swap-remove, so the moves never chain).  Per slot: seed, subsequence,
 // talker and predictor row parameters, a history range of `history_capacity`
 // ids at slot * capacity, its end, and the frame's codes row and status.
-// The talker step commits with a history append (q3s_commit_rows), so the
-// c0 history never leaves the device.
+// Each step is one launch that samples and commits (q3s_sample_commit); the
+// talker step's commit appends the c0 ids, so the history never leaves the
+// device.
 #include <cstdint>
 #include <cstring>
 #include <string>
@@ -423,8 +424,6 @@ int q3s_scheduler_step(q3s_scheduler* q, int32_t group, const void* logits, int3
   }
   b.tokens = q->tokens;
   b.status = q->status;
-  int rc = q3s_sample_batch(q->ctx, &b, stream);
-  if (rc != Q3S_OK) return rc;
   q3s_commit c;
   std::memset(&c, 0, sizeof(c));
   c.num_rows = n;
@@ -442,7 +441,7 @@ int q3s_scheduler_step(q3s_scheduler* q, int32_t group, const void* logits, int3
     c.history_ends = q->s.hend;
     c.history_limits = q->hlim;
   }
-  return q3s_commit_rows(q->ctx, &c, stream);
+  return q3s_sample_commit(q->ctx, &b, &c, stream);
 }
 
 int q3s_scheduler_end_frame(q3s_scheduler* q, uint32_t* codes, uint8_t* status, void* stream) {

@@ -155,7 +155,7 @@ EXPORTED_SYMBOLS = (
     "q3s_commit_rows", "q3s_scheduler_create", "q3s_scheduler_destroy", "q3s_scheduler_add",
     "q3s_scheduler_cancel", "q3s_scheduler_begin_frame", "q3s_scheduler_step",
     "q3s_scheduler_end_frame", "q3s_scheduler_codes", "q3s_scheduler_session_state",
-    "q3s_head_sample",
+    "q3s_head_sample", "q3s_sample_commit",
 )
 
 HEAD_MAX_ROWS = 16
@@ -200,6 +200,8 @@ def load(path: Optional[os.PathLike] = None):
     L.q3s_embed_sum.argtypes = [ctypes.c_void_p, ctypes.POINTER(_EmbedBatch), ctypes.c_void_p]
     L.q3s_commit_rows.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Commit), ctypes.c_void_p]
     L.q3s_head_sample.argtypes = [ctypes.c_void_p, ctypes.POINTER(_HeadBatch), ctypes.c_void_p]
+    L.q3s_sample_commit.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Batch),
+                                    ctypes.POINTER(_Commit), ctypes.c_void_p]
     L.q3s_scheduler_create.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
                                        ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p)]
     L.q3s_scheduler_destroy.argtypes = [ctypes.c_void_p]
@@ -932,3 +934,32 @@ def head_sample(hidden, weight, params, seeds=None, subseqs=None, *, history=Non
     _check(load().q3s_head_sample(ctx.handle, ctypes.byref(hb), ctypes.c_void_p(s)),
            "q3s_head_sample")
     return tokens, status, logits
+
+
+def sample_commit(logits, params, seeds, subseqs, *, codes=None, group: int = 0,
+                  frame_status=None, commit_history=None, history_limits=None, row_offsets=None,
+                  row_vocab=None, vocab: Optional[int] = None, history=None, history_offsets=None,
+                  history_ends=None, ctx: Optional[Context] = None, stream=None, out=None):
+    """sample_batch and commit_rows in one launch (q3s_sample_commit): each
+    row's warp commits the row after storing its result.  commit_history:
+    the history array to append the ids to (normally `history`), with
+    history_ends / history_limits; subseqs are advanced in place."""
+    import torch
+    b, ctx, keep, tokens, status = _build_batch(
+        logits, params, seeds, subseqs, row_offsets=row_offsets, row_vocab=row_vocab,
+        vocab=vocab, history=history, history_offsets=history_offsets, uniform_override=None,
+        debug=False, ctx=ctx, out=out, history_ends=history_ends)
+    c = _Commit()
+    c.subseqs = _dptr(subseqs)
+    c.codes = _dptr(codes)
+    c.codes_stride = codes.stride(0) if codes is not None else 0
+    c.group = int(group)
+    c.frame_status = _dptr(frame_status)
+    c.history = _dptr(commit_history)
+    c.history_ends = _dptr(history_ends) if commit_history is not None else None
+    c.history_limits = _dptr(history_limits)
+    dev = logits.device
+    s = torch.cuda.current_stream(dev).cuda_stream if stream is None else stream
+    _check(load().q3s_sample_commit(ctx.handle, ctypes.byref(b), ctypes.byref(c),
+                                    ctypes.c_void_p(s)), "q3s_sample_commit")
+    return tokens, status

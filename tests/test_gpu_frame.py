@@ -84,14 +84,17 @@ def _frame_inputs(rng, S):
     return talker, cp_bf, pt, pc
 
 
-def test_frames_with_failures_history_and_embedding():
+@pytest.mark.parametrize("fused", [False, True], ids=["sample_then_commit", "sample_commit"])
+def test_frames_with_failures_history_and_embedding(fused):
     """Two frames of 64 streams through the device-side commit: the c0 ids
     join each stream's fixed-capacity history on the device and penalise the
     next frame's talker call; a stream whose code-predictor logits are all
     -inf at group 7 stops there (NO_CANDIDATE), one with an invalid talker
     top_p stops at group 0, and one whose history is full stops with
     HISTORY_FULL after its draw.  The frame's codes then feed the codebook
-    embedding sum straight from the device buffer."""
+    embedding sum straight from the device buffer.  Run with two launches per
+    group (q3s_sample_batch, q3s_commit_rows) and with one
+    (q3s_sample_commit)."""
     rng = np.random.default_rng(11)
     S, HCAP = 64, 512
     fail_cp, fail_topp, full = 5, 9, 13
@@ -127,15 +130,23 @@ def test_frames_with_failures_history_and_embedding():
         pcd = torch.from_numpy(pc.view(np.uint8).copy()).to(DEV)
         xt = torch.from_numpy(talker).to(DEV)
         xc = cp_bf.to(DEV)
-        t, st = q3s.sample_batch(xt, ptd, seeds, subseqs, history=hist, history_offsets=hstart,
-                                 history_ends=hend)
-        q3s.commit_rows(t, st, params=ptd, subseqs=subseqs, codes=codes, group=0,
-                        frame_status=fstat, history=hist, history_ends=hend,
-                        history_limits=hlim)
-        for g in range(1, GROUPS):
-            t, st = q3s.sample_batch(xc[g - 1], pcd, seeds, subseqs)
-            q3s.commit_rows(t, st, params=pcd, subseqs=subseqs, codes=codes, group=g,
-                            frame_status=fstat)
+        if fused:
+            q3s.sample_commit(xt, ptd, seeds, subseqs, codes=codes, group=0, frame_status=fstat,
+                              commit_history=hist, history_limits=hlim, history=hist,
+                              history_offsets=hstart, history_ends=hend)
+            for g in range(1, GROUPS):
+                q3s.sample_commit(xc[g - 1], pcd, seeds, subseqs, codes=codes, group=g,
+                                  frame_status=fstat)
+        else:
+            t, st = q3s.sample_batch(xt, ptd, seeds, subseqs, history=hist,
+                                     history_offsets=hstart, history_ends=hend)
+            q3s.commit_rows(t, st, params=ptd, subseqs=subseqs, codes=codes, group=0,
+                            frame_status=fstat, history=hist, history_ends=hend,
+                            history_limits=hlim)
+            for g in range(1, GROUPS):
+                t, st = q3s.sample_batch(xc[g - 1], pcd, seeds, subseqs)
+                q3s.commit_rows(t, st, params=pcd, subseqs=subseqs, codes=codes, group=g,
+                                frame_status=fstat)
         # The embedding sum reads the frame's codes on the device.
         H = 256
         vocabs = [3072] + [2048] * (GROUPS - 1)
