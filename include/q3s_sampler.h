@@ -328,7 +328,8 @@ int q3s_commit_rows(q3s_context* ctx, const q3s_commit* commit, void* stream);
  * batch's are used); its other fields are as for q3s_commit_rows.  Rows are
  * the batch's rows, so `subseqs` is usually the batch's own subseqs array
  * and the history fields the batch's history, history_ends and a limits
- * array. */
+ * array.  The batch's probs and masks must be NULL, and the context's path
+ * statistics are not collected for these launches. */
 int q3s_sample_commit(q3s_context* ctx, const q3s_batch* batch, const q3s_commit* commit,
                       void* stream);
 

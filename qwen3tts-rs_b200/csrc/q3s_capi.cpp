@@ -207,6 +207,8 @@ int q3s_sample_commit(q3s_context* ctx, const q3s_batch* b, const q3s_commit* c,
   if (b->num_rows == 0) return Q3S_OK;
   int rc = validate_batch(b);
   if (rc != Q3S_OK) return rc;
+  if (b->probs || b->masks)
+    return fail(Q3S_E_INVALID_ARGUMENT, "q3s_sample_commit: no debug outputs (probs, masks)");
   if (c->codes && (c->group < 0 || c->codes_stride <= c->group))
     return fail(Q3S_E_INVALID_ARGUMENT, "q3s_sample_commit: group outside codes_stride");
   if (c->history && (!c->history_ends || !c->history_limits))

@@ -2347,8 +2347,10 @@ general:
 // into the frame's code column; unless the row's frame already failed, the
 // subsequence advanced on a draw, the id appended to the row's history range
 // (HISTORY_FULL when it has no room) and the first failure kept.
-__device__ __noinline__ void commit_row(const KernelArgs& a, long long row, RowOut out,
-                                        bool do_sample) {
+// Inlined: an out-of-line function taking the kernel arguments by reference
+// makes the compiler copy them to local memory for every thread.
+__device__ __forceinline__ void commit_row(const KernelArgs& a, long long row, RowOut out,
+                                           bool do_sample) {
   if (a.c_codes) a.c_codes[row * a.c_codes_stride + a.c_group] = out.token;
   if (a.c_frame_status && a.c_frame_status[row] != Q3S_STATUS_OK) return;
   int st = out.status;
@@ -2369,7 +2371,9 @@ __device__ __noinline__ void commit_row(const KernelArgs& a, long long row, RowO
 // the rows, in the dynamic shared memory `smem` (block_smem bytes).  The
 // sampling kernel runs it with its own block index; the fused head kernel's
 // last block runs it as the one block of a one-block grid.
-template <int DT, int NJ, bool DBG, bool RT>
+// CM: the launch commits each row (q3s_sample_commit); other launches
+// carry no commit code.
+template <int DT, int NJ, bool DBG, bool RT, bool CM = false>
 __device__ __forceinline__ void sample_block(const KernelArgs& a, unsigned char* smem,
                                              const long long bid, const long long G) {
   constexpr int es = Elem<DT>::BYTES;
@@ -2477,7 +2481,7 @@ __device__ __forceinline__ void sample_block(const KernelArgs& a, unsigned char*
     if (lane == 0) {
       a.tokens[row] = out.token;
       a.status[row] = (unsigned char)out.status;
-      if (a.commit) commit_row(a, row, out, (pflags & PF_DO_SAMPLE) != 0u);
+      if constexpr (CM) commit_row(a, row, out, (pflags & PF_DO_SAMPLE) != 0u);
       if (DBG && a.path_stats) {
         atomicAdd(&a.path_stats[path], 1ull);
         atomicAdd(&a.path_stats[Q3S_PATH_COUNT + path], (unsigned long long)(clock64() - clk0));
@@ -2494,10 +2498,10 @@ __device__ __forceinline__ void sample_block(const KernelArgs& a, unsigned char*
         mbar_wait_bounded(&ctl->full[s], ctl->consumed[s] & 1u, WAIT_LIMIT_NS);
 }
 
-template <int DT, int NJ, bool DBG, bool RT>
+template <int DT, int NJ, bool DBG, bool RT, bool CM>
 __global__ void __launch_bounds__(MAX_WARPS * 32, 1) sample_kernel(const KernelArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
-  sample_block<DT, NJ, DBG, RT>(a, smem, blockIdx.x, gridDim.x);
+  sample_block<DT, NJ, DBG, RT, CM>(a, smem, blockIdx.x, gridDim.x);
 }
 
 // Producer fusion: the head projection logits = hidden · Wᵀ of the talker's
@@ -2658,21 +2662,29 @@ cudaError_t ensure_smem(K kernel, std::atomic<int>* set, size_t smem) {
   return e;
 }
 
-template <int DT, int NJ, bool DBG, bool RT>
+template <int DT, int NJ, bool DBG, bool RT, bool CM = false>
 cudaError_t launch_dbg(const KernelArgs& a, int grid, int warps, cudaStream_t stream) {
   static std::atomic<int> smem_set[MAX_DEVICES];
   const size_t smem = block_smem(a.vcap, Elem<DT>::BYTES, warps);
-  cudaError_t e = ensure_smem(sample_kernel<DT, NJ, DBG, RT>, smem_set, smem);
+  cudaError_t e = ensure_smem(sample_kernel<DT, NJ, DBG, RT, CM>, smem_set, smem);
   if (e != cudaSuccess) return e;
-  sample_kernel<DT, NJ, DBG, RT><<<grid, warps * 32, smem, stream>>>(a);
+  sample_kernel<DT, NJ, DBG, RT, CM><<<grid, warps * 32, smem, stream>>>(a);
   return cudaGetLastError();
 }
 
 // Launches with per-row vocabularies run the runtime-chunk kernel when the
 // kernel's chunk holds two or more groups of 8 vectors (a shorter exact row
 // is then possible); all other launches keep the fixed-chunk code.
+// Committing launches (q3s_sample_commit) run their own instantiation,
+// without debug outputs, fixed chunk or runtime chunk as for the others.
 template <int DT, int NJ>
 cudaError_t launch_t(const KernelArgs& a, int grid, int warps, cudaStream_t stream) {
+  if (a.commit) {
+    if constexpr (NJ >= 16) {
+      if (a.row_vocab) return launch_dbg<DT, NJ, false, true, true>(a, grid, warps, stream);
+    }
+    return launch_dbg<DT, NJ, false, false, true>(a, grid, warps, stream);
+  }
   const bool dbg = a.probs || a.masks || a.path_stats;
   if constexpr (NJ >= 16) {
     if (a.row_vocab)
