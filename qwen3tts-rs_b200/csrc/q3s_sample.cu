@@ -2540,30 +2540,39 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, 1)
     float acc[MAX_WARPS];
 #pragma unroll
     for (int r = 0; r < MAX_WARPS; ++r) acc[r] = 0.0f;
-    for (int q = lane; q < Q; q += 32) {
-      const uint4 w4 = __ldg(wrow + q);
-      const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
-      float wv[8];
+    // Four weight vectors per lane in flight, then their products in order.
+    for (int q0 = lane; q0 < Q; q0 += 128) {
+      uint4 w4[4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        wv[2 * t] = __uint_as_float(ww[t] << 16);
-        wv[2 * t + 1] = __uint_as_float(ww[t] & 0xFFFF0000u);
-      }
+      for (int u = 0; u < 4; ++u)
+        w4[u] = q0 + 32 * u < Q ? __ldg(wrow + q0 + 32 * u) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-      for (int r = 0; r < MAX_WARPS; ++r) {
-        if (r < R) {
-          const float4 h0 = *reinterpret_cast<const float4*>(hs + r * H + 8 * q);
-          const float4 h1 = *reinterpret_cast<const float4*>(hs + r * H + 8 * q + 4);
-          float s2 = acc[r];
-          s2 = __fadd_rn(s2, __fmul_rn(wv[0], h0.x));
-          s2 = __fadd_rn(s2, __fmul_rn(wv[1], h0.y));
-          s2 = __fadd_rn(s2, __fmul_rn(wv[2], h0.z));
-          s2 = __fadd_rn(s2, __fmul_rn(wv[3], h0.w));
-          s2 = __fadd_rn(s2, __fmul_rn(wv[4], h1.x));
-          s2 = __fadd_rn(s2, __fmul_rn(wv[5], h1.y));
-          s2 = __fadd_rn(s2, __fmul_rn(wv[6], h1.z));
-          s2 = __fadd_rn(s2, __fmul_rn(wv[7], h1.w));
-          acc[r] = s2;
+      for (int u = 0; u < 4; ++u) {
+        const int q = q0 + 32 * u;
+        if (q >= Q) break;
+        const uint32_t ww[4] = {w4[u].x, w4[u].y, w4[u].z, w4[u].w};
+        float wv[8];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          wv[2 * t] = __uint_as_float(ww[t] << 16);
+          wv[2 * t + 1] = __uint_as_float(ww[t] & 0xFFFF0000u);
+        }
+#pragma unroll
+        for (int r = 0; r < MAX_WARPS; ++r) {
+          if (r < R) {
+            const float4 h0 = *reinterpret_cast<const float4*>(hs + r * H + 8 * q);
+            const float4 h1 = *reinterpret_cast<const float4*>(hs + r * H + 8 * q + 4);
+            float s2 = acc[r];
+            s2 = __fadd_rn(s2, __fmul_rn(wv[0], h0.x));
+            s2 = __fadd_rn(s2, __fmul_rn(wv[1], h0.y));
+            s2 = __fadd_rn(s2, __fmul_rn(wv[2], h0.z));
+            s2 = __fadd_rn(s2, __fmul_rn(wv[3], h0.w));
+            s2 = __fadd_rn(s2, __fmul_rn(wv[4], h1.x));
+            s2 = __fadd_rn(s2, __fmul_rn(wv[5], h1.y));
+            s2 = __fadd_rn(s2, __fmul_rn(wv[6], h1.z));
+            s2 = __fadd_rn(s2, __fmul_rn(wv[7], h1.w));
+            acc[r] = s2;
+          }
         }
       }
     }
