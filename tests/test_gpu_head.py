@@ -104,3 +104,28 @@ def test_head_sample_rejects_bad_shapes():
     w2 = torch.zeros((2048, 1020), dtype=torch.bfloat16, device=DEV)
     with pytest.raises(q3s.LibraryError):
         q3s.head_sample(h2, w2, p, z[:2], z[:2])            # H not a multiple of 8
+
+
+@pytest.mark.parametrize("hdt,pad", [(torch.bfloat16, 4), (torch.float32, 1)])
+def test_head_sample_unaligned_hidden_rows(hdt, pad):
+    """Hidden rows that do not start on 16-byte boundaries (a padded row
+    stride) are staged element by element: the same logits and ids as the
+    contiguous rows, which are staged with 16-byte loads."""
+    R, V, H = 6, 3072, 1024
+    hidden, weight = _inputs(R, V, H, hdt, seed=91)
+    wide = torch.zeros((R, H + pad), dtype=hdt, device=DEV)
+    wide[:, :H] = hidden
+    view = wide[:, :H]
+    assert view.stride(0) == H + pad
+    p, hist, hoff, seeds, subs = _rows(R, V, seed=92, talker=True)
+    dp = torch.from_numpy(p.view(np.uint8).copy()).to(DEV)
+    ds = torch.from_numpy(seeds.view(np.int64)).to(DEV)
+    du = torch.from_numpy(subs.view(np.int64)).to(DEV)
+    kw = {"history": torch.from_numpy(hist.view(np.int16)).to(DEV),
+          "history_offsets": torch.from_numpy(hoff).to(DEV)}
+    a = q3s.head_sample(hidden, weight, dp, ds, du, **kw)
+    b = q3s.head_sample(view, weight, dp, ds, du, **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(a[2], b[2])
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    _check_logits(hidden, weight, b[2])
