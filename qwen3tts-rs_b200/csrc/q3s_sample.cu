@@ -1433,9 +1433,11 @@ __device__ __forceinline__ unsigned long long pack_out(int status, uint32_t toke
 }
 
 // exp(x) for x <= 0 (finite or -inf): cr_expf without the NaN and overflow
-// branches, which such arguments never take; same operations otherwise.
+// branches, which such arguments never take; same operations otherwise.  The
+// underflow case (x < -104, exp(x) rounds to 0) is a select after the
+// arithmetic, not a branch around it, so that the independent calls of a
+// lane (the nucleus path's four per 16-byte vector) interleave.
 __device__ __forceinline__ float cr_expf_nonpos(float xf) {
-  if (xf < -104.0f) return 0.0f;
   const double x = (double)xf;
   // rint(x / ln2) by the 1.5 * 2^52 addition (round to nearest even, exact
   // for |x / ln2| < 2^51); k is the low word of the sum.
@@ -1459,7 +1461,8 @@ __device__ __forceinline__ float cr_expf_nonpos(float xf) {
   p = __fma_rn(p, r, 1.0);
   const int k = __double2loint(big);
   const double scale = __hiloint2double((k + 1023) << 20, 0);
-  return __double2float_rn(__dmul_rn(p, scale));
+  const float e = __double2float_rn(__dmul_rn(p, scale));
+  return xf < -104.0f ? 0.0f : e;
 }
 
 // Shared-memory vector load and store through the shared window (32-bit
